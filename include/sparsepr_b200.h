@@ -1,0 +1,176 @@
+/*
+ * sparsepr_b200 — C ABI of the B200-native SparsePR attention hot path.
+ *
+ * Every entry point is stream-ordered on `stream` (a cudaStream_t passed as
+ * void*), performs no host<->device synchronisation and allocates no memory:
+ * outputs and scratch ("workspace") belong to the caller, who sizes scratch
+ * with the matching *_workspace_bytes query.  All pointers are device
+ * pointers unless stated.  Tensors are dense, row-major, last dimension
+ * contiguous; "bh" is batch*heads.
+ *
+ * Return value: SPR_OK (0) or a negative SPR_ERR_* status; the message of the
+ * last failure on the calling host thread is available from spr_last_error().
+ *
+ * Each declaration cites the reference interface it replaces (paths relative
+ * to the SparsePR project root).
+ */
+#ifndef SPARSEPR_B200_H
+#define SPARSEPR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SPR_OK = 0,
+  SPR_ERR_SHAPE = -1,
+  SPR_ERR_DTYPE = -2,
+  SPR_ERR_ALIGN = -3,
+  SPR_ERR_LAUNCH = -4,
+  SPR_ERR_TIMEOUT = -5,
+  SPR_ERR_UNIMPLEMENTED = -6,
+  SPR_ERR_WORKSPACE = -7,
+  SPR_ERR_ARG = -8
+};
+
+/* Element type codes for `*_dtype` arguments. */
+enum { SPR_F32 = 0, SPR_BF16 = 1, SPR_F16 = 2 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int spr_version(void);
+/* Message of the last failed call on this host thread ("" if none). */
+const char* spr_last_error(void);
+
+/* ---------------------------------------------------------------- k-means */
+
+/* Scratch bytes needed by spr_kmeans_lloyd / spr_label_sort for a problem. */
+size_t spr_kmeans_workspace_bytes(int64_t bh, int64_t n, int d, int k);
+
+/*
+ * Batched Lloyd k-means, `iters` iterations with an on-device stop when the
+ * max L2 centroid shift falls below `tol` (later iterations become no-ops).
+ * x [bh,n,d] (x_dtype), centroids_inout [bh,k,d] fp32 (initial in, final out).
+ * Outputs (for the last assignment): labels [bh,n] i32, sizes [bh,k] i32,
+ * offsets [bh,k+1] i32 (exclusive prefix of sizes), order [bh,n] i32 (token
+ * ids sorted by label, ties by token id), iters_done [1] i32.
+ * centroid_round_dtype: SPR_F32, or x_dtype to round updated centroids to the
+ * storage type each iteration like the standalone flash_kmeans path.
+ * Replaces: src/sparsepr/kmeans_utils.py:1504-1580 batch_kmeans_Euclid(backend="flash")
+ *   -> 1281-1465 (assign kmeans_utils.py:775-893 / flash_kmeans/assign_euclid_triton.py:803-1412,
+ *   update flash_kmeans/centroid_update_triton.py:316-386, sizes kmeans_utils.py:1110-1157),
+ *   and flash_kmeans/kmeans_triton_impl.py:55-115.
+ */
+int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
+                     int iters, float tol, int centroid_round_dtype,
+                     float* centroids_inout, int32_t* labels, int32_t* sizes,
+                     int32_t* offsets, int32_t* order, int32_t* iters_done,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One assignment step: labels[b,i] = argmin_j max(|x|^2+|c_j|^2-2 x.c_j, 0),
+ * ties to the lowest j.  Replaces flash_kmeans/assign_euclid_triton.py:1238-1412
+ * euclid_assign_triton.
+ */
+int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
+                      const float* centroids, int32_t* labels, void* stream);
+
+/*
+ * Stable counting sort of labels: sizes [bh,k], offsets [bh,k+1], order [bh,n].
+ * Replaces the torch.argsort(labels) of src/sparsepr/models/common/n8_v6.py:905 and
+ * src/sparsepr/adapters/wan22.py:2031 plus _cluster_sizes_from_labels (kmeans_utils.py:1110-1157).
+ */
+int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
+                   int32_t* offsets, int32_t* order, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * Segmented mean over the label-sorted order, fused with the permute:
+ * means[b,c,:] = mean of x[b, order[b, offsets[b,c]:offsets[b,c+1]], :] in fp32,
+ * empty clusters take fallback[b,c,:] (or 0 when fallback is NULL);
+ * when x_perm != NULL also writes x_perm[b,s,:] = x[b,order[b,s],:].
+ * Replaces models/cosmos3/operator_kmeans.py:609-679 (original_centroids,
+ * joint_original_centroids -> kernels/triton/centroid_reduction.py:138-196) and
+ * kernels/triton/permute.py:126-172 permute_tensor_by_labels_triton.
+ */
+int spr_centroid_means(const void* x, int x_dtype, const int32_t* order, const int32_t* offsets,
+                       int64_t bh, int64_t n, int d, int k, const float* fallback, float* means,
+                       void* x_perm, void* stream);
+
+/*
+ * Row permute of [bh,n,d] elements of elem_bytes each: inverse==0 gathers
+ * y[b,s]=x[b,idx[b,s]]; inverse==1 scatters y[b,idx[b,s]]=x[b,s].
+ * Replaces kernels/triton/permute.py:126-172 and 235-274 (apply_inverse_permutation_triton).
+ */
+int spr_permute_rows(const void* x, const int32_t* idx, void* y, int64_t bh, int64_t n, int d,
+                     int elem_bytes, int inverse, void* stream);
+
+/* ---------------------------------------------------------------- routing */
+
+/*
+ * Attention-mass selector scores: scores[b,q,c] = log sum_{t in cluster c}
+ * exp(qc[b,q].k_sorted[b,t] / sqrt(d)), -inf for empty clusters.
+ * q_centroids [bh,cq,d] fp32, k_sorted [bh,n,d] bf16, k_offsets [bh,ck+1] i32.
+ * Replaces kernels/triton/svg_ear.py:372-450 attention_mass_scores_triton (kernel 7-92).
+ */
+int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets,
+                              int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream);
+
+/*
+ * Budgeted cluster selection per (b, q): descending score (ties -> lower
+ * cluster id), keep the positive-size prefix within budgets[b,q], plus the
+ * first crossing cluster.  routed [bh,cq+1,ck+1] u8 (nullable; header row/col
+ * as the reference), sel_ids [bh,cq,ck] i32 ascending selected cluster ids
+ * (-1 padded), sel_counts [bh,cq] i32.  ck <= 2048.
+ * Replaces kernels/triton/selector_budget.py:131-171 exact_budget_dynamic_map_triton and
+ * kernels/n8_ext/csrc/n8_ops.cu:271-355 (svg_ear_select_budget_schedule, compact_selected_clusters).
+ */
+int spr_select_budget(const float* scores, const int32_t* k_sizes, const int32_t* budgets,
+                      int64_t bh, int cq, int ck, uint8_t* routed, int32_t* sel_ids,
+                      int32_t* sel_counts, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/*
+ * Block-sparse attention over kept cluster pairs, bf16 in, fp32 accumulate:
+ * for query row s of q-cluster c (rows q_offsets[b,c]..q_offsets[b,c+1] of
+ * q_perm), softmax(q.K^T/sqrt(d)) V over the key rows of the clusters
+ * sel_ids[b,c,0:sel_counts[b,c]] (runs k_offsets[b,j]..k_offsets[b,j+1] of
+ * k_perm/v_perm).  Rows with no keys output 0.  q_perm [bh,nq,d],
+ * k_perm/v_perm [bh,nk,d] bf16, d == 128.  When q_order != NULL the row is
+ * stored at out[b, q_order[b,s]] (fused inverse permute), else at out[b,s].
+ * Replaces src/sparsepr/kmeans_utils.py:2164-2350 dynamic_block_sparse_fwd_flashinfer
+ * (+ its plan() index build) and kernels/triton/permute.py:235-274.
+ */
+int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_perm,
+                          const int32_t* q_offsets, const int32_t* k_offsets,
+                          const int32_t* sel_ids, const int32_t* sel_counts,
+                          int64_t bh, int64_t nq, int64_t nk, int d, int cq, int ck,
+                          const int32_t* q_order, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Scratch bytes needed by spr_block_sparse_attn. */
+size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq);
+
+/* ---------------------------------------------------------------- repair */
+
+/*
+ * Apply the reduced-rank residual repair and overwrite probe rows:
+ * out[b,i] = base[b,i] + alpha*((((base[b,i]-x_mean)/x_scale) L) B^T + y_mean),
+ * then out[b, rows[b,m]] = dense[b,m].  base/out [bh,n,d] bf16 (may alias),
+ * x_mean/x_scale/y_mean [bh,d] fp32, left/basis [bh,d,r] fp32, rows [bh,m] i32,
+ * dense [bh,m,d] bf16.  Replaces kernels/triton/residual_repair.py:388-562
+ * n8_repair_apply_output_triton and 656-700 n8_exact_probe_scatter_triton.
+ */
+int spr_repair_apply(const void* base, const float* x_mean, const float* x_scale, const float* y_mean,
+                     const float* left, const float* basis, int64_t bh, int64_t n, int d, int r,
+                     float alpha, const int32_t* rows, const void* dense, int m, void* out,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSEPR_B200_H */

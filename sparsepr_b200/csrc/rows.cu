@@ -1,0 +1,131 @@
+// Row-level HBM kernels: permute / inverse permute, repair apply with the
+// exact probe-row overwrite, and the library's error/version plumbing.
+#include "common.cuh"
+
+namespace spr {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+// Each warp moves rows with 16-byte accesses; `cpr` chunks per row.
+__global__ void permute_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ idx,
+                                    uint4* __restrict__ y, int64_t n, int cpr, int inverse, int64_t total_rows) {
+  const int lane = threadIdx.x & 31;
+  const int rpw = 32 / cpr;
+  const int sub = lane / cpr, ch = lane % cpr;
+  if (sub >= rpw) return;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp * rpw + sub; r < total_rows; r += nwarps * rpw) {
+    const int64_t b = r / n;
+    const int64_t t = idx[r];
+    const int64_t src = inverse ? r : b * n + t;
+    const int64_t dst = inverse ? b * n + t : r;
+    y[dst * cpr + ch] = x[src * cpr + ch];
+  }
+}
+
+// Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym)); one warp per row.
+template <int D, int R>
+__global__ void __launch_bounds__(256)
+repair_apply_kernel(const __nv_bfloat16* __restrict__ base, const float* __restrict__ xm,
+                    const float* __restrict__ xs, const float* __restrict__ ym, const float* __restrict__ left,
+                    const float* __restrict__ basis, int64_t n, float alpha, __nv_bfloat16* __restrict__ out) {
+  __shared__ float sh_l[D * R], sh_b[D * R], sh_xm[D], sh_xs[D], sh_ym[D];
+  const int64_t b = blockIdx.y;
+  for (int i = threadIdx.x; i < D * R; i += blockDim.x) {
+    sh_l[i] = left[b * D * R + i];
+    sh_b[i] = basis[b * D * R + i];
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    sh_xm[i] = xm[b * D + i];
+    sh_xs[i] = xs[b * D + i];
+    sh_ym[i] = ym[b * D + i];
+  }
+  __syncthreads();
+  constexpr int PER = D / 32;  // dims per lane (contiguous)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rows_per_block = blockDim.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * rows_per_block + warp; r < n; r += (int64_t)gridDim.x * rows_per_block) {
+    const __nv_bfloat16* br = base + (b * n + r) * D + lane * PER;
+    float v[PER], z[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      v[e] = __bfloat162float(br[e]);
+      const int dd = lane * PER + e;
+      z[e] = (v[e] - sh_xm[dd]) / sh_xs[dd];
+    }
+    float coord[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      float p = 0.f;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) p = fmaf(z[e], sh_l[(lane * PER + e) * R + j], p);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+      coord[j] = p;
+    }
+    __nv_bfloat16* orow = out + (b * n + r) * D + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const int dd = lane * PER + e;
+      float c = sh_ym[dd];
+#pragma unroll
+      for (int j = 0; j < R; ++j) c = fmaf(coord[j], sh_b[dd * R + j], c);
+      orow[e] = __float2bfloat16(v[e] + alpha * c);
+    }
+  }
+}
+
+// Overwrite probe rows with their exact dense attention output.
+__global__ void probe_scatter_kernel(const int32_t* __restrict__ rows, const uint4* __restrict__ dense, int m,
+                                     int64_t n, int cpr, uint4* __restrict__ out) {
+  const int64_t b = blockIdx.y;
+  const int j = blockIdx.x;
+  const int64_t r = rows[b * m + j];
+  for (int c = threadIdx.x; c < cpr; c += blockDim.x) out[(b * n + r) * cpr + c] = dense[(b * m + j) * (int64_t)cpr + c];
+}
+
+}  // namespace spr
+
+using namespace spr;
+
+extern "C" int spr_version(void) { return 100; }
+extern "C" const char* spr_last_error(void) { return g_last_error; }
+
+extern "C" int spr_permute_rows(const void* x, const int32_t* idx, void* y, int64_t bh, int64_t n, int d,
+                                int elem_bytes, int inverse, void* stream) {
+  const int64_t rb = (int64_t)d * elem_bytes;
+  if (bh <= 0 || n <= 0 || rb % 16 != 0 || rb / 16 > 32)
+    return fail(SPR_ERR_SHAPE, "permute: row of %lld bytes unsupported", (long long)rb);
+  if (!aligned(x, 16) || !aligned(y, 16)) return fail(SPR_ERR_ALIGN, "permute: 16-byte alignment required");
+  const int64_t rows = bh * n;
+  const int blocks = (int)std::min<int64_t>((rows + 7) / 8, 148 * 16);
+  permute_rows_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const uint4*)x, idx, (uint4*)y, n, (int)(rb / 16),
+                                                                inverse, rows);
+  return check_launch("permute");
+}
+
+extern "C" int spr_repair_apply(const void* base, const float* x_mean, const float* x_scale, const float* y_mean,
+                                const float* left, const float* basis, int64_t bh, int64_t n, int d, int r,
+                                float alpha, const int32_t* rows, const void* dense, int m, void* out, void* stream) {
+  if (d != 128 || r != 16) return fail(SPR_ERR_SHAPE, "repair apply: requires d=128, r=16 (got d=%d r=%d)", d, r);
+  if (bh <= 0 || n <= 0 || bh > 65535) return fail(SPR_ERR_SHAPE, "repair apply: bad shape");
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid((unsigned)std::min<int64_t>((n + 7) / 8, 4096), (unsigned)bh);
+  repair_apply_kernel<128, 16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)base, x_mean, x_scale, y_mean, left, basis,
+                                                     n, alpha, (__nv_bfloat16*)out);
+  int s = check_launch("repair apply");
+  if (s) return s;
+  if (rows && dense && m > 0) {
+    probe_scatter_kernel<<<dim3((unsigned)m, (unsigned)bh), 32, 0, st>>>(rows, (const uint4*)dense, m, n, 16, (uint4*)out);
+    return check_launch("probe scatter");
+  }
+  return SPR_OK;
+}

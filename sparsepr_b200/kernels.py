@@ -1,0 +1,207 @@
+"""Torch-tensor wrappers over the C ABI (device memory and streams come from PyTorch).
+
+Every function checks shapes/dtypes/devices, allocates its outputs with
+``torch.empty`` on the input's device, and launches on the current CUDA
+stream.  There is no CPU path: non-CUDA inputs raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.SPR_F32, torch.bfloat16: _lib.SPR_BF16, torch.float16: _lib.SPR_F16}
+_WS: dict[tuple, torch.Tensor] = {}
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _cuda(*ts: torch.Tensor) -> torch.device:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"sparsepr_b200 kernels need CUDA tensors, got a {t.device} tensor")
+    return ts[0].device
+
+
+def _contig(name: str, t: torch.Tensor) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous, got strides {t.stride()}")
+    return t
+
+
+def workspace(dev: torch.device, nbytes: int, tag: str = "default") -> torch.Tensor:
+    """Caller-owned scratch, cached per (device, tag) and grown on demand."""
+    key = (dev.type, dev.index, tag)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor) -> torch.Tensor:
+    """Nearest centroid per point (ties -> lowest index): x [B,N,D], c [B,K,D] fp32 -> int32 [B,N]."""
+    dev = _cuda(x, centroids)
+    b, n, d = x.shape
+    k = centroids.shape[1]
+    if centroids.shape != (b, k, d) or centroids.dtype != torch.float32:
+        raise RuntimeError(f"centroids must be fp32 [B,K,D]={b, k, d}, got {tuple(centroids.shape)} {centroids.dtype}")
+    labels = torch.empty((b, n), dtype=torch.int32, device=dev)
+    _lib.call("spr_kmeans_assign", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, _p(_contig("centroids", centroids)),
+              _p(labels), _stream(dev))
+    return labels
+
+
+def kmeans_lloyd(x: torch.Tensor, init_centroids: torch.Tensor, iters: int, tol: float = 0.0,
+                 round_centroids_to_input: bool = False):
+    """Batched Lloyd k-means with an on-device ``tol`` stop.
+
+    Returns ``(labels i32 [B,N], centroids f32 [B,K,D], sizes i32 [B,K],
+    offsets i32 [B,K+1], order i32 [B,N], iters_done i32 [1] device tensor)``.
+    """
+    dev = _cuda(x, init_centroids)
+    b, n, d = x.shape
+    k = init_centroids.shape[1]
+    if init_centroids.shape != (b, k, d):
+        raise RuntimeError(f"init centroids must be [B,K,D]={b, k, d}, got {tuple(init_centroids.shape)}")
+    cent = init_centroids.to(torch.float32).contiguous().clone()
+    labels = torch.empty((b, n), dtype=torch.int32, device=dev)
+    sizes = torch.empty((b, k), dtype=torch.int32, device=dev)
+    offsets = torch.empty((b, k + 1), dtype=torch.int32, device=dev)
+    order = torch.empty((b, n), dtype=torch.int32, device=dev)
+    iters_done = torch.zeros((1,), dtype=torch.int32, device=dev)
+    nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
+    ws = workspace(dev, nbytes, "kmeans")
+    rd = _DT[x.dtype] if round_centroids_to_input else _lib.SPR_F32
+    _lib.call("spr_kmeans_lloyd", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, int(iters), float(tol), rd,
+              _p(cent), _p(labels), _p(sizes), _p(offsets), _p(order), _p(iters_done), _p(ws), ws.numel(),
+              _stream(dev))
+    return labels, cent, sizes, offsets, order, iters_done
+
+
+def label_sort(labels: torch.Tensor, k: int):
+    """Stable counting sort: (sizes i32 [B,K], offsets i32 [B,K+1], order i32 [B,N])."""
+    dev = _cuda(labels)
+    if labels.dtype != torch.int32:
+        raise RuntimeError("labels must be int32")
+    b, n = labels.shape
+    sizes = torch.empty((b, k), dtype=torch.int32, device=dev)
+    offsets = torch.empty((b, k + 1), dtype=torch.int32, device=dev)
+    order = torch.empty((b, n), dtype=torch.int32, device=dev)
+    nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, 16, k)
+    ws = workspace(dev, nbytes, "kmeans")
+    _lib.call("spr_label_sort", _p(_contig("labels", labels)), b, n, k, _p(sizes), _p(offsets), _p(order), _p(ws),
+              ws.numel(), _stream(dev))
+    return sizes, offsets, order
+
+
+def centroid_means(x: torch.Tensor, order: torch.Tensor, offsets: torch.Tensor, k: int,
+                   fallback: torch.Tensor | None = None, permute: bool = False):
+    """Per-cluster fp32 means over the sorted order, optionally emitting the permuted x."""
+    dev = _cuda(x, order, offsets)
+    b, n, d = x.shape
+    means = torch.empty((b, k, d), dtype=torch.float32, device=dev)
+    x_perm = torch.empty_like(x) if permute else None
+    if fallback is not None:
+        fallback = fallback.to(torch.float32).contiguous()
+        if fallback.shape != (b, k, d):
+            raise RuntimeError(f"fallback must be [B,K,D]={b, k, d}")
+    _lib.call("spr_centroid_means", _p(_contig("x", x)), _DT[x.dtype], _p(order), _p(offsets), b, n, d, k,
+              _p(fallback), _p(means), _p(x_perm), _stream(dev))
+    return means, x_perm
+
+
+def permute_rows(x: torch.Tensor, idx: torch.Tensor, inverse: bool = False) -> torch.Tensor:
+    """Gather ``y[b,s]=x[b,idx[b,s]]`` (or scatter when ``inverse``) over [B,N,D] rows."""
+    dev = _cuda(x, idx)
+    b, n, d = x.shape
+    y = torch.empty_like(x)
+    _lib.call("spr_permute_rows", _p(_contig("x", x)), _p(_contig("idx", idx)), _p(y), b, n, d, x.element_size(),
+              int(inverse), _stream(dev))
+    return y
+
+
+def attention_mass_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, k_offsets: torch.Tensor) -> torch.Tensor:
+    """log-sum-exp attention mass per (query centroid, key cluster) -> fp32 [B,Cq,Ck]."""
+    dev = _cuda(q_centroids, k_sorted, k_offsets)
+    b, cq, d = q_centroids.shape
+    ck = k_offsets.shape[1] - 1
+    n = k_sorted.shape[1]
+    if k_sorted.dtype != torch.bfloat16:
+        raise RuntimeError("k_sorted must be bf16")
+    qc = q_centroids.float().contiguous()
+    scores = torch.empty((b, cq, ck), dtype=torch.float32, device=dev)
+    _lib.call("spr_attention_mass_scores", _p(qc), _p(_contig("k_sorted", k_sorted)),
+              _p(_contig("k_offsets", k_offsets)), b, cq, ck, n, d, _p(scores), _stream(dev))
+    return scores
+
+
+def select_budget(scores: torch.Tensor, k_sizes: torch.Tensor, budgets: torch.Tensor):
+    """Budgeted selection -> (routed bool [B,Cq+1,Ck+1], sel_ids i32 [B,Cq,Ck], sel_counts i32 [B,Cq])."""
+    dev = _cuda(scores, k_sizes, budgets)
+    b, cq, ck = scores.shape
+    routed = torch.empty((b, cq + 1, ck + 1), dtype=torch.bool, device=dev)
+    ids = torch.empty((b, cq, ck), dtype=torch.int32, device=dev)
+    counts = torch.empty((b, cq), dtype=torch.int32, device=dev)
+    ks = k_sizes.to(torch.int32).contiguous()
+    bu = budgets.to(torch.int32).contiguous()
+    _lib.call("spr_select_budget", _p(_contig("scores", scores)), _p(ks), _p(bu), b, cq, ck, _p(routed), _p(ids),
+              _p(counts), _stream(dev))
+    return routed, ids, counts
+
+
+def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
+                           q_order: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-sparse attention over kept cluster pairs (bf16, d=128) -> [B,Nq,D] bf16."""
+    dev = _cuda(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts)
+    b, nq, d = q_perm.shape
+    nk = k_perm.shape[1]
+    cq = q_offsets.shape[1] - 1
+    ck = k_offsets.shape[1] - 1
+    for name, t in (("q_perm", q_perm), ("k_perm", k_perm), ("v_perm", v_perm)):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"{name} must be bf16, got {t.dtype}")
+        _contig(name, t)
+    if out is None:
+        out = torch.empty_like(q_perm)
+    nbytes = _lib.query("spr_block_sparse_attn_workspace_bytes", b, nq, cq)
+    ws = workspace(dev, nbytes, "attn")
+    _lib.call("spr_block_sparse_attn", _p(q_perm), _p(k_perm), _p(v_perm), _p(q_offsets), _p(k_offsets), _p(sel_ids),
+              _p(sel_counts), b, nq, nk, d, cq, ck, _p(q_order), _p(out), _p(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def dense_attention_rows(q_rows: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Exact attention of [B,M,D] query rows against all [B,N,D] keys (one cluster pair)."""
+    dev = _cuda(q_rows, k, v)
+    b, m, _ = q_rows.shape
+    n = k.shape[1]
+    q_off = torch.tensor([0, m], dtype=torch.int32, device=dev).expand(b, 2).contiguous()
+    k_off = torch.tensor([0, n], dtype=torch.int32, device=dev).expand(b, 2).contiguous()
+    ids = torch.zeros((b, 1, 1), dtype=torch.int32, device=dev)
+    cnt = torch.ones((b, 1), dtype=torch.int32, device=dev)
+    return block_sparse_attention(q_rows.contiguous(), k, v, q_off, k_off, ids, cnt)
+
+
+def repair_apply(base: torch.Tensor, state, alpha: float, rows: torch.Tensor | None = None,
+                 dense: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reduced-rank residual repair + probe overwrite on bf16 [B,N,128] (rank 16)."""
+    dev = _cuda(base)
+    x_mean, x_scale, y_mean, left, basis = (t.to(torch.float32).contiguous() for t in state)
+    b, n, d = base.shape
+    r = left.shape[-1]
+    if out is None:
+        out = torch.empty_like(base)
+    m = 0 if rows is None else rows.shape[1]
+    rows_i = None if rows is None else rows.to(torch.int32).contiguous()
+    dense_b = None if dense is None else dense.to(torch.bfloat16).contiguous()
+    _lib.call("spr_repair_apply", _p(_contig("base", base)), _p(x_mean), _p(x_scale), _p(y_mean), _p(left), _p(basis),
+              b, n, d, r, float(alpha), _p(rows_i), _p(dense_b), m, _p(out), _stream(dev))
+    return out
