@@ -1,0 +1,22 @@
+"""sparsepr_b200: B200-native (sm_100a) SparsePR sparse-attention hot path.
+
+Public API:
+
+* :class:`N8V6Config`, :class:`N8V6Core`, :class:`N8V6Route` — the routing +
+  repair core (drop-in for ``sparsepr.models.common.n8_v6``).
+* :func:`sparse_attention` — the adapter-facing attention call.
+* :func:`batch_kmeans_Euclid`, :class:`FlashKMeans` — standalone batched k-means.
+* :mod:`sparsepr_b200.kernels` — tensor wrappers over the C ABI.
+"""
+
+from .n8_v6 import N8V6Config, N8V6Core, N8V6Route  # noqa: F401
+from .attention import (  # noqa: F401
+    Wan22TI2VSparseConfig,
+    install_wan22_ti2v_sparse_patch,
+    kept_flops,
+    make_n8_core,
+    sparse_attention,
+)
+from .kmeans import FlashKMeans, batch_kmeans_Euclid  # noqa: F401
+
+__version__ = "0.1.0"

@@ -1,0 +1,140 @@
+"""The adapter-facing SparsePR attention call and the Wan2.2 drop-in hook.
+
+``sparse_attention`` mirrors ``_sparse_n8_attention_bhld``
+(``src/sparsepr/adapters/wan22.py:1945-2182``): route, block-sparse
+attention over the kept cluster pairs (stored straight back to the original
+token order), then probe repair.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import kernels as K
+from .n8_v6 import N8V6Config, N8V6Core
+
+__all__ = ["sparse_attention", "Wan22TI2VSparseConfig", "install_wan22_ti2v_sparse_patch", "make_n8_core",
+           "kept_flops", "sparse_n8_attention_bhld"]
+
+
+def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, **route_kw):
+    """One SparsePR attention call on [B,H,N,D] Q/K/V.
+
+    Returns ``(repaired [B,H,N,D] bf16, density float, info dict)`` like the
+    reference's ``(repaired, density, timings)``.  ``info['route']`` holds the
+    route for callers that audit it.
+    """
+    if q.ndim != 4:
+        raise RuntimeError(f"sparse_attention expects [B,H,N,D] tensors, got {tuple(q.shape)}.")
+    batch, heads, tokens, dim = q.shape
+    if batch != 1:
+        raise RuntimeError("Wan2.2 N8 currently requires batch size one.")
+    route = core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
+                       **route_kw)
+    bh = batch * heads
+    base = K.block_sparse_attention(
+        route.q_permuted, route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim),
+        route.q_offsets, route.k_offsets, route.selected_ids, route.selected_counts,
+        q_order=route.q_sorted_indices)
+    repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
+    info["route"] = route
+    return repaired, float(info["effective_video_density"]), info
+
+
+def kept_flops(route, head_dim: int, probe_rows: int, tokens: int) -> torch.Tensor:
+    """Kept FLOPs ``4*D*(selected_pairs + probe_pairs)`` as a device scalar
+    (the reference FLOP audit, ``src/sparsepr/adapters/wan22.py:183-190, 2044-2065``)."""
+    mask = route.video_dynamic_map
+    sel_keys = (mask.long() * route.k_cluster_sizes.long().unsqueeze(1)).sum(-1)
+    pairs = (sel_keys * route.q_cluster_sizes.long()).sum()
+    probe_pairs = mask.shape[0] * probe_rows * tokens
+    return 4 * head_dim * (pairs + probe_pairs)
+
+
+@dataclass
+class Wan22TI2VSparseConfig:
+    """N8 fields of ``src/sparsepr/adapters/wan22.py:22-57`` used by the core."""
+
+    num_q_centroids: int = 300
+    num_k_centroids: int = 1000
+    kmeans_iter_init: int = 50
+    kmeans_iter_step: int = 2
+    n8_target_density: float = 0.22
+    n8_probe_rows: int = 64
+    n8_repair_rank: int = 16
+    n8_role_q_rank: int = 64
+    n8_role_k_rank: int = 48
+    n8_role_v_rank: int = 16
+    n8_role_v_weight: float = 0.0
+    n8_metric_sample_tokens: int = 2048
+    n8_factor_power_iters: int = 2
+    n8_factor_refresh_every: int = 1
+    n8_role_kv_matmul_precision: str = "high"
+    n8_selector_policy: str = "attention_mass"
+
+
+_CONFIG = Wan22TI2VSparseConfig()
+
+
+def make_n8_core(cfg: Wan22TI2VSparseConfig | None = None) -> N8V6Core:
+    """``_make_n8_core`` (``wan22.py:1515-1548``) on this build."""
+    c = cfg or _CONFIG
+    return N8V6Core(N8V6Config(
+        num_q_centroids=int(c.num_q_centroids), num_k_centroids=int(c.num_k_centroids),
+        target_density=float(c.n8_target_density), role_q_rank=int(c.n8_role_q_rank),
+        role_k_rank=int(c.n8_role_k_rank), role_v_rank=int(c.n8_role_v_rank),
+        role_v_weight=float(c.n8_role_v_weight), metric_sample_tokens=int(c.n8_metric_sample_tokens),
+        kmeans_iter_init=int(c.kmeans_iter_init), kmeans_iter_step=int(c.kmeans_iter_step),
+        factor_power_iters=int(c.n8_factor_power_iters), factor_refresh_every=int(c.n8_factor_refresh_every),
+        probe_rows=int(c.n8_probe_rows), repair_rank=int(c.n8_repair_rank),
+        selector_policy=str(c.n8_selector_policy), role_kv_matmul_precision=str(c.n8_role_kv_matmul_precision),
+    ))
+
+
+def _core_for_cfg_branch(attn) -> N8V6Core:
+    """Branch-local core per CFG pass (``wan22.py:1551-1566``)."""
+    branch = int(getattr(attn, "_svg_cfg_branch", 0))
+    cores = getattr(attn, "_n8_cores", None)
+    if not isinstance(cores, dict):
+        cores = {}
+        attn._n8_cores = cores
+    core = cores.get(branch)
+    if core is None:
+        core = make_n8_core()
+        cores[branch] = core
+    attn._n8_core = core
+    return core
+
+
+def sparse_n8_attention_bhld(attn, q_bhld, k_bhld, v_bhld, seq_lens=None):
+    """Drop-in body of ``_sparse_n8_attention_bhld``: returns ``(repaired, density, timings)``."""
+    del seq_lens
+    core = _core_for_cfg_branch(attn)
+    out, density, info = sparse_attention(q_bhld, k_bhld, v_bhld, core)
+    info.pop("route", None)
+    dtype = v_bhld.dtype if v_bhld.dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
+    return out.to(dtype), density, info
+
+
+def install_wan22_ti2v_sparse_patch(config: Wan22TI2VSparseConfig | None = None, module=None):
+    """Install this build behind ``--attention sparsepr``.
+
+    ``module`` is the reference adapter module (``sparsepr.adapters.wan22``);
+    its ``_sparse_n8_attention_bhld`` is replaced by
+    :func:`sparse_n8_attention_bhld` and its ``_make_n8_core`` by
+    :func:`make_n8_core`, so the reference's Wan attention override routes
+    every sparse call through sparsepr_b200.  Returns the previous functions.
+    """
+    global _CONFIG
+    if config is not None:
+        _CONFIG = config
+    if module is None:
+        import importlib
+
+        module = importlib.import_module("sparsepr.adapters.wan22")
+    previous = (getattr(module, "_sparse_n8_attention_bhld", None), getattr(module, "_make_n8_core", None))
+    module._sparse_n8_attention_bhld = sparse_n8_attention_bhld
+    module._make_n8_core = make_n8_core
+    return previous

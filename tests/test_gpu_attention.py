@@ -1,0 +1,164 @@
+"""Block-sparse attention, dense probe rows, repair and the full SparsePR call
+against the CPU oracle.  Tolerance (bf16 outputs): max-abs <= 2e-2 and
+cosine >= 0.999 per head."""
+
+import types
+
+import pytest
+import torch
+
+import oracle
+from sparsepr_b200 import N8V6Config, N8V6Core, kernels as K, sparse_attention
+from sparsepr_b200.synthetic import synthetic_qkv
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+COS = 0.999
+
+
+def _close(got, ref):
+    got, ref = got.float().cpu(), ref.float().cpu()
+    err = (got - ref).abs().max().item()
+    assert err <= ATOL, err
+    for h in range(got.shape[0]):
+        a, b = got[h].flatten(), ref[h].flatten()
+        if b.norm() > 0:
+            assert torch.nn.functional.cosine_similarity(a, b, dim=0).item() >= COS
+
+
+def _random_layout(g, bh, n, cq, ck, density):
+    def sizes_for(c):
+        lab = torch.randint(0, c, (bh, n), generator=g)
+        lab[:, : n // 5] = 0  # one big cluster
+        return torch.zeros(bh, c, dtype=torch.long).scatter_add_(1, lab, torch.ones_like(lab))
+
+    qs, ks = sizes_for(cq), sizes_for(ck)
+    mask = torch.rand(bh, cq, ck, generator=g) < density
+    mask[:, 1] = False  # a query cluster with no keys -> zero rows
+    return qs, ks, mask
+
+
+def _i32(t, dev):
+    return t.to(torch.int32).to(dev)
+
+
+@pytest.mark.parametrize("n,cq,ck,density", [(700, 9, 23, 0.3), (4096, 31, 120, 0.25), (257, 3, 5, 1.0)])
+def test_block_sparse_attention_matches_oracle(cuda, n, cq, ck, density):
+    g = torch.Generator().manual_seed(n)
+    bh = 3
+    q, k, v = (torch.randn(bh, n, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    qs, ks, mask = _random_layout(g, bh, n, cq, ck, density)
+    ref = oracle.block_sparse_attention(q, k, v, mask, qs, ks)
+    ids, cnt = oracle.compact_selected(mask)
+    got = K.block_sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), _i32(oracle.cluster_offsets(qs), cuda),
+                                   _i32(oracle.cluster_offsets(ks), cuda), _i32(ids, cuda), _i32(cnt, cuda))
+    _close(got, ref)
+    qo = oracle.cluster_offsets(qs)
+    assert got[:, int(qo[0, 1]):int(qo[0, 2])].abs().max().item() == 0.0  # key-less cluster -> zeros
+
+
+def test_block_sparse_fused_inverse_store(cuda):
+    g = torch.Generator().manual_seed(5)
+    bh, n, cq, ck = 2, 1500, 12, 40
+    q, k, v = (torch.randn(bh, n, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    qs, ks, mask = _random_layout(g, bh, n, cq, ck, 0.3)
+    order = torch.stack([torch.randperm(n, generator=g) for _ in range(bh)])
+    ids, cnt = oracle.compact_selected(mask)
+    args = (q.to(cuda), k.to(cuda), v.to(cuda), _i32(oracle.cluster_offsets(qs), cuda),
+            _i32(oracle.cluster_offsets(ks), cuda), _i32(ids, cuda), _i32(cnt, cuda))
+    plain = K.block_sparse_attention(*args)
+    fused = K.block_sparse_attention(*args, q_order=_i32(order, cuda))
+    assert torch.equal(fused.cpu(), oracle.inverse_permute_rows(plain.cpu(), order))
+
+
+@pytest.mark.parametrize("m,n", [(64, 5000), (7, 129), (16, 64)])
+def test_dense_rows_match_oracle(cuda, m, n):
+    g = torch.Generator().manual_seed(m)
+    q = torch.randn(2, m, 128, generator=g).to(torch.bfloat16)
+    k, v = (torch.randn(2, n, 128, generator=g).to(torch.bfloat16) for _ in range(2))
+    _close(K.dense_attention_rows(q.to(cuda), k.to(cuda), v.to(cuda)), oracle.dense_attention_rows(q, k, v))
+
+
+def test_repair_apply_matches_oracle(cuda):
+    g = torch.Generator().manual_seed(9)
+    bh, n, m = 2, 3000, 64
+    base = torch.randn(bh, n, 128, generator=g).to(torch.bfloat16)
+    x = torch.gather(base.float(), 1, torch.randint(0, n, (bh, m, 1), generator=g).expand(-1, -1, 128))
+    y = 0.1 * torch.randn(bh, m, 128, generator=g)
+    w = torch.rand(bh, m, generator=g) + 0.5
+    state = oracle.fit_reduced_rank_residual(x, y, w / w.mean(1, keepdim=True), 16, 0.1)
+    rows = torch.stack([torch.randperm(n, generator=g)[:m] for _ in range(bh)])
+    dense = torch.randn(bh, m, 128, generator=g).to(torch.bfloat16)
+    ref = oracle.repair_apply(base, state)
+    ref.scatter_(1, rows.unsqueeze(2).expand(-1, -1, 128), dense)
+    got = K.repair_apply(base.to(cuda), tuple(t.to(cuda) for t in state), 1.0, rows.to(cuda), dense.to(cuda))
+    _close(got, ref)
+
+
+def _cfg(**kw):
+    base = dict(num_q_centroids=32, num_k_centroids=48, target_density=0.3, kmeans_iter_init=6, probe_rows=32,
+                repair_rank=16, selector_policy="attention_mass", role_kv_matmul_precision="highest", kmeans_tol=0.0)
+    base.update(kw)
+    return N8V6Config(**base)
+
+
+def _oracle_cfg(cfg):
+    return types.SimpleNamespace(**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__})
+
+
+def test_route_matches_oracle(cuda):
+    """Route stages against the oracle from the same initial-centroid indices."""
+    cfg = _cfg()
+    q, k, v = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
+    core = N8V6Core(cfg)
+    r = core.route(q.to(cuda), k.to(cuda), v.to(cuda))
+    ro = oracle.oracle_route(q, k, v, _oracle_cfg(cfg), init_seed=0, tol=0.0)
+    agree_k = (r.k_labels.cpu().long() == ro.k_labels).float().mean().item()
+    agree_q = (r.q_labels.cpu().long() == ro.q_labels).float().mean().item()
+    assert agree_k > 0.97 and agree_q > 0.97, (agree_k, agree_q)
+    # Given the build's own labels, every later stage matches the oracle.
+    kl, ql = r.k_labels.cpu().long(), r.q_labels.cpu().long()
+    ks, qs = r.k_cluster_sizes.cpu().long(), r.q_cluster_sizes.cpu().long()
+    k3, q3 = k.view(2, -1, 128), q.view(2, -1, 128)
+    assert torch.equal(r.k_sorted_indices.cpu().long(), oracle.stable_label_order(kl))
+    kperm = oracle.permute_rows(k3, oracle.stable_label_order(kl))
+    assert torch.equal(r.k_permuted.view(2, -1, 128).cpu(), kperm)
+    qcent = oracle.original_centroids(q3, ql, qs)
+    torch.testing.assert_close(core.q_centroids.cpu(), qcent, atol=1e-5, rtol=1e-5)
+    sc = oracle.attention_mass_scores(qcent, kperm, ks)
+    fin = torch.isfinite(sc)
+    torch.testing.assert_close(r.scores.cpu()[fin], sc[fin], atol=2e-4, rtol=1e-5)
+    routed = oracle.select_budget(r.scores.cpu(), ks, r.budgets.cpu())
+    assert torch.equal(r.video_dynamic_map.cpu(), routed[:, 1:, 1:])
+
+
+def _route_view(r, bh):
+    return types.SimpleNamespace(
+        q_labels=r.q_labels.cpu().long(), q_sizes=r.q_cluster_sizes.cpu().long(),
+        k_sizes=r.k_cluster_sizes.cpu().long(), mask=r.video_dynamic_map.cpu(), q_features=r.q_role_features.cpu(),
+        q_order=r.q_sorted_indices.cpu().long(), k_perm=r.k_permuted.view(bh, -1, 128).cpu(),
+        v_perm=r.v_permuted.view(bh, -1, 128).cpu())
+
+
+def test_sparse_attention_matches_oracle_on_same_route(cuda):
+    cfg = _cfg()
+    q, k, v = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
+    out, density, info = sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg))
+    r = info["route"]
+    ref, _route, _base, (_state, rows, _w, _dense) = oracle.oracle_sparse_attention(
+        q, k, v, _oracle_cfg(cfg), route=_route_view(r, 2))
+    assert torch.equal(r.probe_rows.cpu(), rows)
+    _close(out.view(2, -1, 128), ref.view(2, -1, 128))
+    assert 0.0 < density <= 1.0
+
+
+def test_warm_second_call_runs(cuda):
+    cfg = _cfg(kmeans_iter_step=2)
+    q, k, v = (t.to(cuda) for t in synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16))
+    core = N8V6Core(cfg)
+    out1, _, _ = sparse_attention(q, k, v, core)
+    out2, _, info = sparse_attention(q, k, v, core)
+    assert info["route"].q_kmeans_iters == 2
+    assert torch.isfinite(out2.float()).all()
+    assert torch.nn.functional.cosine_similarity(out1.float().flatten(), out2.float().flatten(), dim=0) > 0.99

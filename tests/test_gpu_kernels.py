@@ -1,0 +1,148 @@
+"""Parity of each CUDA kernel (through the C ABI) against the CPU oracle."""
+
+import pytest
+import torch
+
+import oracle
+from sparsepr_b200 import kernels as K
+from sparsepr_b200.synthetic import synthetic_kmeans_points
+
+pytestmark = pytest.mark.gpu
+
+
+def _near_tie_free(x, c):
+    """Points whose best/second-best gap exceeds an fp32 rounding bound."""
+    gap = oracle.assign_margin(x, c)
+    scale = (x.double() ** 2).sum(-1) + (c.double() ** 2).sum(-1).max(-1, keepdim=True).values
+    return gap > 1e-5 * scale
+
+
+@pytest.mark.parametrize("d,dtype", [(48, torch.float32), (64, torch.float32), (128, torch.bfloat16), (16, torch.float32)])
+def test_assign_matches_oracle(cuda, d, dtype):
+    g = torch.Generator().manual_seed(d)
+    x = torch.randn(3, 1537, d, generator=g).to(dtype)
+    c = torch.randn(3, 77, d, generator=g)
+    ref = oracle.euclid_assign(x, c)
+    got = K.kmeans_assign(x.to(cuda), c.to(cuda)).cpu().long()
+    ok = _near_tie_free(x, c)
+    assert ok.float().mean() > 0.95
+    assert torch.equal(got[ok], ref[ok])
+
+
+def test_assign_ties_go_to_lowest_index(cuda):
+    x = torch.zeros(1, 64, 16)
+    c = torch.zeros(1, 200, 16)  # every centroid equidistant
+    assert K.kmeans_assign(x.to(cuda), c.to(cuda)).max().item() == 0
+
+
+@pytest.mark.parametrize("n,k", [(1, 1), (5000, 7), (70001, 1000), (4097, 3000)])
+def test_label_sort_is_stable_counting_sort(cuda, n, k):
+    g = torch.Generator().manual_seed(n)
+    labels = torch.randint(0, k, (2, n), generator=g, dtype=torch.int32)
+    labels[1, : n // 2] = 0  # skewed cluster sizes
+    sizes, offsets, order = K.label_sort(labels.to(cuda), k)
+    ref_sizes = torch.zeros(2, k, dtype=torch.long).scatter_add_(1, labels.long(), torch.ones(2, n, dtype=torch.long))
+    assert torch.equal(order.cpu().long(), oracle.stable_label_order(labels))
+    assert torch.equal(sizes.cpu().long(), ref_sizes)
+    assert torch.equal(offsets.cpu().long(), oracle.cluster_offsets(ref_sizes))
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float32, 48), (torch.float32, 64)])
+def test_centroid_means_and_permute(cuda, dtype, d):
+    g = torch.Generator().manual_seed(7)
+    n, k = 3001, 50
+    x = torch.randn(2, n, d, generator=g).to(dtype)
+    labels = torch.randint(0, k - 5, (2, n), generator=g, dtype=torch.int32)  # last 5 clusters empty
+    fallback = torch.randn(2, k, d, generator=g)
+    sizes, offsets, order = K.label_sort(labels.to(cuda), k)
+    means, xp = K.centroid_means(x.to(cuda), order, offsets, k, fallback.to(cuda), permute=True)
+    ref = oracle.original_centroids(x, labels, sizes.cpu().long(), fallback)
+    torch.testing.assert_close(means.cpu(), ref, atol=1e-5, rtol=1e-5)
+    assert torch.equal(xp.cpu(), oracle.permute_rows(x, oracle.stable_label_order(labels)))
+
+
+def test_permute_inverse_round_trip(cuda):
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(3, 999, 128, generator=g).to(torch.bfloat16).to(cuda)
+    idx = torch.stack([torch.randperm(999, generator=g) for _ in range(3)]).to(torch.int32).to(cuda)
+    y = K.permute_rows(x, idx)
+    assert torch.equal(y.cpu(), oracle.permute_rows(x.cpu(), idx.cpu()))
+    assert torch.equal(K.permute_rows(y, idx, inverse=True), x)
+
+
+def test_kmeans_lloyd_matches_oracle(cuda):
+    x = synthetic_kmeans_points(2, 64, (4, 12, 16), 24, dtype=torch.float32, seed=5)
+    init = x[:, torch.randperm(x.shape[1], generator=torch.Generator().manual_seed(1))[:24]].clone()
+    lr, cr, sr, itr = oracle.batch_kmeans_euclid(x, 24, 6, 0.0, init)
+    l, c, s, off, order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 6, 0.0)
+    assert it.item() == itr == 6
+    assert (l.cpu().long() == lr).float().mean() > 0.999
+    if torch.equal(l.cpu().long(), lr):
+        torch.testing.assert_close(c.cpu(), cr, atol=1e-4, rtol=1e-4)
+        assert torch.equal(s.cpu().long(), sr)
+        assert torch.equal(order.cpu().long(), oracle.stable_label_order(lr))
+
+
+def test_kmeans_tol_stops_on_device(cuda):
+    x = synthetic_kmeans_points(1, 32, (2, 8, 8), 8, dtype=torch.float32, seed=2)
+    init = x[:, :8].clone()
+    _l, _c, _s, itr = oracle.batch_kmeans_euclid(x, 8, 40, 1e-3, init)
+    _l2, _c2, _s2, _off, _order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 40, 1e-3)
+    assert it.item() == itr < 40
+
+
+def test_kmeans_bf16_rounded_centroids(cuda):
+    x = synthetic_kmeans_points(2, 128, (3, 10, 12), 16, dtype=torch.bfloat16, seed=4)
+    init = x[:, :16].float().clone()
+    lr, _cr, _sr, _ = oracle.batch_kmeans_euclid(x, 16, 4, 0.0, init, centroid_dtype=torch.bfloat16)
+    l, c, *_ = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 4, 0.0, round_centroids_to_input=True)
+    assert (l.cpu().long() == lr).float().mean() > 0.999
+    assert torch.equal(c.cpu().to(torch.bfloat16).float(), c.cpu())
+
+
+def test_attention_mass_scores(cuda):
+    g = torch.Generator().manual_seed(11)
+    bh, n, cq, ck = 2, 1200, 40, 33
+    k = torch.randn(bh, n, 128, generator=g).to(torch.bfloat16)
+    lab = torch.randint(0, ck - 3, (bh, n), generator=g)
+    sizes = torch.zeros(bh, ck, dtype=torch.long).scatter_add_(1, lab, torch.ones_like(lab))
+    qc = torch.randn(bh, cq, 128, generator=g)
+    ref = oracle.attention_mass_scores(qc, k, sizes)
+    off = oracle.cluster_offsets(sizes).to(torch.int32).to(cuda)
+    got = K.attention_mass_scores(qc.to(cuda), k.to(cuda), off).cpu()
+    fin = torch.isfinite(ref)
+    assert torch.equal(fin, torch.isfinite(got))
+    torch.testing.assert_close(got[fin], ref[fin], atol=2e-4, rtol=1e-5)
+
+
+def test_selector_known_answer(cuda):
+    """tests/test_n8_extension.py:79-103 of the reference, through the C ABI."""
+    scores = torch.tensor([[[4.0, 3.0, 2.0, 1.0], [1.0, 4.0, 3.0, 2.0]]], device=cuda)
+    sizes = torch.tensor([[2, 3, 5, 1]], device=cuda, dtype=torch.int32)
+    budgets = torch.tensor([[6, 4]], device=cuda, dtype=torch.int32)
+    routed, ids, counts = K.select_budget(scores, sizes, budgets)
+    expected = torch.tensor([[True, True, True, False], [False, True, True, False]], device=cuda)
+    assert torch.equal(routed[0, 1:, 1:], expected)
+    assert routed[0, 0, 0].item() and routed[0, 1:, 0].all().item()
+    assert not routed[0, 0, 1:].any().item()
+    assert counts.tolist() == [[3, 2]]
+    assert ids[0, 0, :3].tolist() == [0, 1, 2] and ids[0, 1, :2].tolist() == [1, 2]
+
+
+@pytest.mark.parametrize("ck", [1, 37, 1000, 2048])
+def test_selector_matches_oracle_bit_exact(cuda, ck):
+    g = torch.Generator().manual_seed(ck)
+    bh, cq = 3, 17
+    scores = torch.randn(bh, cq, ck, generator=g)
+    scores[:, :, ::7] = scores[:, :, :1]  # ties
+    sizes = torch.randint(0, 50, (bh, ck), generator=g)
+    scores = torch.where(sizes.unsqueeze(1) > 0, scores, torch.full_like(scores, float("-inf")))
+    budgets = torch.randint(0, int(sizes.sum(1).max()) + 10, (bh, cq), generator=g)
+    budgets[0, 0] = 0
+    ref = oracle.select_budget(scores, sizes, budgets)
+    routed, ids, counts = K.select_budget(scores.to(cuda), sizes.to(torch.int32).to(cuda),
+                                          budgets.to(torch.int32).to(cuda))
+    assert torch.equal(routed.cpu(), ref)
+    rid, rcnt = oracle.compact_selected(ref[:, 1:, 1:])
+    assert torch.equal(counts.cpu(), rcnt)
+    assert torch.equal(ids.cpu(), rid)
