@@ -40,6 +40,8 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
         q_order=route.q_sorted_indices)
     repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
     info["route"] = route
+    info["base"] = base
+    info["repair_state"] = core.repair_state_current
     return repaired, float(info["effective_video_density"]), info
 
 
@@ -113,7 +115,8 @@ def sparse_n8_attention_bhld(attn, q_bhld, k_bhld, v_bhld, seq_lens=None):
     del seq_lens
     core = _core_for_cfg_branch(attn)
     out, density, info = sparse_attention(q_bhld, k_bhld, v_bhld, core)
-    info.pop("route", None)
+    for key in ("route", "base", "repair_state"):
+        info.pop(key, None)
     dtype = v_bhld.dtype if v_bhld.dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
     return out.to(dtype), density, info
 

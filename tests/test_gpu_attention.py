@@ -55,7 +55,8 @@ def test_block_sparse_attention_matches_oracle(cuda, n, cq, ck, density):
                                    _i32(oracle.cluster_offsets(ks), cuda), _i32(ids, cuda), _i32(cnt, cuda))
     _close(got, ref)
     qo = oracle.cluster_offsets(qs)
-    assert got[:, int(qo[0, 1]):int(qo[0, 2])].abs().max().item() == 0.0  # key-less cluster -> zeros
+    for h in range(bh):  # key-less cluster -> zeros
+        assert got[h, int(qo[h, 1]):int(qo[h, 2])].abs().max().item() == 0.0
 
 
 def test_block_sparse_fused_inverse_store(cuda):
@@ -142,15 +143,43 @@ def _route_view(r, bh):
 
 
 def test_sparse_attention_matches_oracle_on_same_route(cuda):
+    """Base attention on the build's route within tolerance; the repaired output
+    against the oracle's apply of the same fitted state (the 32-probe rank-16
+    fit itself is compared separately: its top-16 subspace is sensitive to
+    last-bit differences between eigensolvers)."""
     cfg = _cfg()
     q, k, v = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
     out, density, info = sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg))
     r = info["route"]
-    ref, _route, _base, (_state, rows, _w, _dense) = oracle.oracle_sparse_attention(
+    _ref, _route, base_ref, (_state, rows, _w, dense) = oracle.oracle_sparse_attention(
         q, k, v, _oracle_cfg(cfg), route=_route_view(r, 2))
     assert torch.equal(r.probe_rows.cpu(), rows)
-    _close(out.view(2, -1, 128), ref.view(2, -1, 128))
+    base = info["base"].cpu()
+    _close(base, base_ref)
+    state = tuple(t.cpu() for t in info["repair_state"])
+    ref = oracle.repair_apply(base, state)
+    ref.scatter_(1, rows.unsqueeze(2).expand(-1, -1, 128), dense)
+    _close(out.view(2, -1, 128), ref)
     assert 0.0 < density <= 1.0
+
+
+def test_repair_fit_matches_oracle(cuda):
+    """The fitted correction operator L B^T, means and scales on a well-conditioned fit."""
+    from sparsepr_b200.n8_v6 import fit_reduced_rank_residual
+
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(4, 64, 128, generator=g)
+    y = torch.randn(4, 64, 16, generator=g) @ torch.randn(4, 16, 128, generator=g) * 0.3
+    y = y + 0.01 * torch.randn(4, 64, 128, generator=g)
+    w = torch.rand(4, 64, generator=g) + 0.5
+    w = w / w.mean(1, keepdim=True)
+    ref = oracle.fit_reduced_rank_residual(x, y, w, 16, 0.1)
+    got = [t.cpu() for t in fit_reduced_rank_residual(x.to(cuda), y.to(cuda), w.to(cuda), 16, 0.1)]
+    for i in range(3):
+        torch.testing.assert_close(got[i], ref[i], atol=1e-4, rtol=1e-4)
+    op_ref = ref[3] @ ref[4].transpose(1, 2)
+    op_got = got[3] @ got[4].transpose(1, 2)
+    torch.testing.assert_close(op_got, op_ref, atol=1e-3 * op_ref.abs().max().item(), rtol=1e-3)
 
 
 def test_warm_second_call_runs(cuda):
