@@ -1,0 +1,287 @@
+"""Benchmark: one SparsePR attention layer at the Wan2.2-720p shape (config 3).
+
+Step = one cold ``sparse_attention`` call on 75,600 tokens x 40 heads x 128
+(bf16): role factors, K and Q Lloyd k-means (10 iterations each), centroid
+means + permutes, attention-mass scores, budgeted selection (keep 30% of
+key tokens per query cluster), block-sparse attention, 64 dense probe rows,
+rank-16 repair.  Heads are sharded across ranks (``--gpus N`` under torchrun);
+no collective runs on the data path.
+
+Metric: kept TFLOP/s = 4*D*(selected_pairs + probe_pairs) / layer time, the
+reference's FLOP audit (``src/sparsepr/adapters/wan22.py:183-190``), summed
+over ranks; ``ms_per_step`` is the layer latency (max over ranks).
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle restatement under ``oracle/``; the reference itself is Python and does
+not travel to the GPU box) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "SparsePR attn layer ms + kept-TFLOPS at 75.6K tok/40 heads, 1/2/4/8 B200"
+CONFIGS = {
+    3: dict(grid=(21, 45, 80), heads=40, name="wan2.2-720p-81f layer (config 3)"),
+    2: dict(grid=(21, 30, 52), heads=40, name="wan2.2-480p-81f layer (config 2)"),
+}
+SPARSE = dict(num_q_centroids=200, num_k_centroids=1000, target_density=0.3, kmeans_iter_init=10,
+              probe_rows=64, repair_rank=16, repair_ridge=0.1, selector_policy="attention_mass",
+              selector_budget_mode="fixed_density", kmeans_tol=0.0)
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks / throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                      "-i", str(self.index)], capture_output=True, text=True, timeout=5).stdout
+                f = [x.strip() for x in out.strip().split(",")]
+                if len(f) == 6:
+                    self.samples.append(f)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[2:]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.samples[0][1]) if self.samples[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    from sparsepr_b200 import N8V6Config, N8V6Core, kernels as K, sparse_attention
+    from sparsepr_b200.attention import kept_flops
+    from sparsepr_b200.synthetic import synthetic_qkv
+
+    world, rank, local = _dist()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    cfgd = CONFIGS[args.config]
+    heads = cfgd["heads"]
+    if heads % world:
+        raise SystemExit(f"{heads} heads do not shard over {world} GPUs")
+    local_heads = heads // world
+    grid = cfgd["grid"]
+    n = grid[0] * grid[1] * grid[2]
+    # Synthetic Q/K/V for this rank's heads, generated on the device (seeded per rank).
+    seeds = (1000 * rank, 1000 * rank + 1, 1000 * rank + 2)
+    q, k, v = synthetic_qkv(local_heads, 128, grid, dtype=torch.bfloat16, device=dev, seeds=seeds)
+    cfg = N8V6Config(**SPARSE)
+
+    def step(qq, kk, vv, events=None):
+        core = N8V6Core(cfg)  # cold call: full k-means from the seeded init every step
+        return sparse_attention(qq, kk, vv, core, attn_events=events)
+
+    for _ in range(args.warmup):
+        out, _, info = step(q, k, v)
+    torch.cuda.synchronize(dev)
+    kept = int(kept_flops(info["route"], 128, cfg.probe_rows, n).item())
+    route = info["route"]
+    sel_keys = (route.video_dynamic_map.long() * route.k_cluster_sizes.long().unsqueeze(1)).sum(-1)
+    attn_flops = int((4 * 128 * (sel_keys * route.q_cluster_sizes.long()).sum()).item())
+    del out, info, route
+
+    # Device-resident timed region.
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = K.LAUNCHES[0]
+    with ClockSampler(dev.index) as clocks:
+        t0.record()
+        for i in range(args.steps):
+            out, _, info = step(q, k, v, ev[i])
+            del out, info
+        t1.record()
+        torch.cuda.synchronize(dev)
+    launches = (K.LAUNCHES[0] - launches0) // max(args.steps, 1)
+    ms = t0.elapsed_time(t1) / args.steps
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        dist.barrier()
+
+    # End to end through the public API: pinned host inputs -> device, output -> host, every step.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(hq.shape, dtype=torch.bfloat16).pin_memory()
+    del q, k, v
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 3))
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(e_steps):
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        out, _, info = step(dq, dk, dv)
+        hout.copy_(out, non_blocking=True)
+        del out, info, dq, dk, dv
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    h2d = 3 * hq.numel() * 2
+    d2h = hout.numel() * 2
+
+    stats = torch.tensor([ms, e2e_ms, attn_ms, kept, attn_flops], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, e2e_ms, attn_ms = mx[0].item(), mx[1].item(), mx[2].item()
+        kept, attn_flops = sm[3].item(), sm[4].item()
+        h2d *= world
+        d2h *= world
+    if rank == 0:
+        burst, sustained, hbm, src = _peaks()
+        per_rank_attn_flops = attn_flops / world
+        achieved = per_rank_attn_flops / (attn_ms * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": kept / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded smooth-field Q/K + noise, V~N(0,1); no public dataset for this path)",
+            "config": {"workload": cfgd["name"], "tokens": n, "heads": heads, "head_dim": 128,
+                       "heads_per_gpu": local_heads, "q_clusters": 200, "k_clusters": 1000,
+                       "lloyd_iters": 10, "keep": "30% of key tokens per query cluster (fixed_density 0.3)",
+                       "probe_rows": 64, "repair_rank": 16, "parallelism": f"heads-sharded x{world}",
+                       "l2": "inputs (3 x 774 MB bf16 per 40 heads) exceed the 126 MB L2; no flush"},
+            "kept_tflop_per_step": kept / 1e12,
+            "e2e": {"value": kept / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "roofline": {"kernel": "block_sparse_attn_kernel", "bound": "tensor", "achieved": achieved,
+                         "peak": sustained, "peak_source": f"bf16_tflops_sustained ({src})", "unit": "TFLOP/s",
+                         "frac": achieved / sustained, "traffic": None, "attn_ms": attn_ms,
+                         "attn_share_of_step": attn_ms / ms},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, heads_sample=2)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(args, heads_sample: int = 2):
+    """The oracle (CPU restatement of the reference algorithm) on a bounded sample:
+    the same layer on ``heads_sample`` of the 40 heads, scaled to kept TFLOP/s."""
+    import types
+
+    import oracle
+    from sparsepr_b200.synthetic import synthetic_qkv
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfgd = CONFIGS[args.config]
+    grid = cfgd["grid"]
+    n = grid[0] * grid[1] * grid[2]
+    q, k, v = synthetic_qkv(heads_sample, 128, grid, dtype=torch.bfloat16, seeds=(11, 12, 13))
+    oc = types.SimpleNamespace(role_q_rank=64, role_k_rank=48, metric_sample_tokens=2048, repair_alpha=1.0,
+                               repair_norm_cap=0.0, svg_ear_top_p=0.85, adaptive_budget_min_density=0.0,
+                               adaptive_budget_max_density=1.0, **SPARSE)
+    t = time.perf_counter()
+    _out, r, _base, _ = oracle.oracle_sparse_attention(q, k, v, oc, init_seed=0, tol=0.0)
+    dt = time.perf_counter() - t
+    kept = 4 * 128 * (oracle.kept_pairs(r.mask, r.q_sizes, r.k_sizes) + heads_sample * SPARSE["probe_rows"] * n)
+    return {"value": kept / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{heads_sample} of {cfgd['heads']} heads of {cfgd['name']}, full route+attention+repair, "
+                      f"{dt:.1f} s", "seconds": dt, "ms_per_layer_extrapolated": dt * 1e3 * cfgd["heads"] / heads_sample}
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    res = []
+    for _ in range(args.warmup + args.steps if args.steps < 3 else args.steps):
+        res.append(cpu_baseline(args, heads_sample=1))
+    v = statistics.median(x["value"] for x in res[-args.steps:])
+    cb = dict(res[-1])
+    cb["value"] = v
+    cfgd = CONFIGS[args.config]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": cb["ms_per_layer_extrapolated"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (CPU)", "data": "synthetic",
+        "config": {"workload": cfgd["name"], "tokens": cfgd["grid"][0] * cfgd["grid"][1] * cfgd["grid"][2],
+                   "heads": cfgd["heads"], "sample_heads": 1},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -19,12 +19,15 @@ __all__ = ["sparse_attention", "Wan22TI2VSparseConfig", "install_wan22_ti2v_spar
            "kept_flops", "sparse_n8_attention_bhld"]
 
 
-def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, **route_kw):
+def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, attn_events=None,
+                     **route_kw):
     """One SparsePR attention call on [B,H,N,D] Q/K/V.
 
     Returns ``(repaired [B,H,N,D] bf16, density float, info dict)`` like the
-    reference's ``(repaired, density, timings)``.  ``info['route']`` holds the
-    route for callers that audit it.
+    reference's ``(repaired, density, timings)``.  ``info`` also holds the
+    ``route``, the pre-repair ``base`` output and the ``repair_state``.
+    ``attn_events`` (optional pair of ``torch.cuda.Event``) brackets the
+    block-sparse attention launch on the current stream.
     """
     if q.ndim != 4:
         raise RuntimeError(f"sparse_attention expects [B,H,N,D] tensors, got {tuple(q.shape)}.")
@@ -34,10 +37,14 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     route = core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
                        **route_kw)
     bh = batch * heads
+    if attn_events is not None:
+        attn_events[0].record()
     base = K.block_sparse_attention(
         route.q_permuted, route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim),
         route.q_offsets, route.k_offsets, route.selected_ids, route.selected_counts,
         q_order=route.q_sorted_indices)
+    if attn_events is not None:
+        attn_events[1].record()
     repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
     info["route"] = route
     info["base"] = base

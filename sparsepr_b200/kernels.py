@@ -14,6 +14,14 @@ from . import _lib
 _DT = {torch.float32: _lib.SPR_F32, torch.bfloat16: _lib.SPR_BF16, torch.float16: _lib.SPR_F16}
 _WS: dict[tuple, torch.Tensor] = {}
 
+# Number of sparsepr_b200 kernels launched through this module (per process);
+# bench.py reports the count inside its timed region.
+LAUNCHES = [0]
+
+
+def _count(n: int) -> None:
+    LAUNCHES[0] += int(n)
+
 
 def _p(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
@@ -54,6 +62,7 @@ def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor) -> torch.Tensor:
     if centroids.shape != (b, k, d) or centroids.dtype != torch.float32:
         raise RuntimeError(f"centroids must be fp32 [B,K,D]={b, k, d}, got {tuple(centroids.shape)} {centroids.dtype}")
     labels = torch.empty((b, n), dtype=torch.int32, device=dev)
+    _count(1)
     _lib.call("spr_kmeans_assign", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, _p(_contig("centroids", centroids)),
               _p(labels), _stream(dev))
     return labels
@@ -80,6 +89,7 @@ def kmeans_lloyd(x: torch.Tensor, init_centroids: torch.Tensor, iters: int, tol:
     nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
     ws = workspace(dev, nbytes, "kmeans")
     rd = _DT[x.dtype] if round_centroids_to_input else _lib.SPR_F32
+    _count(6 * int(iters))
     _lib.call("spr_kmeans_lloyd", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, int(iters), float(tol), rd,
               _p(cent), _p(labels), _p(sizes), _p(offsets), _p(order), _p(iters_done), _p(ws), ws.numel(),
               _stream(dev))
@@ -97,6 +107,7 @@ def label_sort(labels: torch.Tensor, k: int):
     order = torch.empty((b, n), dtype=torch.int32, device=dev)
     nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, 16, k)
     ws = workspace(dev, nbytes, "kmeans")
+    _count(3)
     _lib.call("spr_label_sort", _p(_contig("labels", labels)), b, n, k, _p(sizes), _p(offsets), _p(order), _p(ws),
               ws.numel(), _stream(dev))
     return sizes, offsets, order
@@ -113,6 +124,7 @@ def centroid_means(x: torch.Tensor, order: torch.Tensor, offsets: torch.Tensor, 
         fallback = fallback.to(torch.float32).contiguous()
         if fallback.shape != (b, k, d):
             raise RuntimeError(f"fallback must be [B,K,D]={b, k, d}")
+    _count(1)
     _lib.call("spr_centroid_means", _p(_contig("x", x)), _DT[x.dtype], _p(order), _p(offsets), b, n, d, k,
               _p(fallback), _p(means), _p(x_perm), _stream(dev))
     return means, x_perm
@@ -123,6 +135,7 @@ def permute_rows(x: torch.Tensor, idx: torch.Tensor, inverse: bool = False) -> t
     dev = _cuda(x, idx)
     b, n, d = x.shape
     y = torch.empty_like(x)
+    _count(1)
     _lib.call("spr_permute_rows", _p(_contig("x", x)), _p(_contig("idx", idx)), _p(y), b, n, d, x.element_size(),
               int(inverse), _stream(dev))
     return y
@@ -138,6 +151,7 @@ def attention_mass_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, k_o
         raise RuntimeError("k_sorted must be bf16")
     qc = q_centroids.float().contiguous()
     scores = torch.empty((b, cq, ck), dtype=torch.float32, device=dev)
+    _count(1)
     _lib.call("spr_attention_mass_scores", _p(qc), _p(_contig("k_sorted", k_sorted)),
               _p(_contig("k_offsets", k_offsets)), b, cq, ck, n, d, _p(scores), _stream(dev))
     return scores
@@ -152,6 +166,7 @@ def select_budget(scores: torch.Tensor, k_sizes: torch.Tensor, budgets: torch.Te
     counts = torch.empty((b, cq), dtype=torch.int32, device=dev)
     ks = k_sizes.to(torch.int32).contiguous()
     bu = budgets.to(torch.int32).contiguous()
+    _count(1)
     _lib.call("spr_select_budget", _p(_contig("scores", scores)), _p(ks), _p(bu), b, cq, ck, _p(routed), _p(ids),
               _p(counts), _stream(dev))
     return routed, ids, counts
@@ -173,6 +188,7 @@ def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids
         out = torch.empty_like(q_perm)
     nbytes = _lib.query("spr_block_sparse_attn_workspace_bytes", b, nq, cq)
     ws = workspace(dev, nbytes, "attn")
+    _count(2)
     _lib.call("spr_block_sparse_attn", _p(q_perm), _p(k_perm), _p(v_perm), _p(q_offsets), _p(k_offsets), _p(sel_ids),
               _p(sel_counts), b, nq, nk, d, cq, ck, _p(q_order), _p(out), _p(ws), ws.numel(), _stream(dev))
     return out
@@ -202,6 +218,7 @@ def repair_apply(base: torch.Tensor, state, alpha: float, rows: torch.Tensor | N
     m = 0 if rows is None else rows.shape[1]
     rows_i = None if rows is None else rows.to(torch.int32).contiguous()
     dense_b = None if dense is None else dense.to(torch.bfloat16).contiguous()
+    _count(1 if m == 0 else 2)
     _lib.call("spr_repair_apply", _p(_contig("base", base)), _p(x_mean), _p(x_scale), _p(y_mean), _p(left), _p(basis),
               b, n, d, r, float(alpha), _p(rows_i), _p(dense_b), m, _p(out), _stream(dev))
     return out

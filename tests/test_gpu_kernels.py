@@ -134,7 +134,7 @@ def test_selector_matches_oracle_bit_exact(cuda, ck):
     g = torch.Generator().manual_seed(ck)
     bh, cq = 3, 17
     scores = torch.randn(bh, cq, ck, generator=g)
-    scores[:, :, ::7] = scores[:, :, :1]  # ties
+    scores[:, :, ::7] = scores[:, :, :1].clone()  # ties
     sizes = torch.randint(0, 50, (bh, ck), generator=g)
     scores = torch.where(sizes.unsqueeze(1) > 0, scores, torch.full_like(scores, float("-inf")))
     budgets = torch.randint(0, int(sizes.sum(1).max()) + 10, (bh, cq), generator=g)
