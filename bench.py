@@ -112,7 +112,9 @@ def run_b200(args):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)
-    cfgd = CONFIGS[args.config]
+    cfgd = dict(CONFIGS[args.config])
+    if args.heads:
+        cfgd["heads"] = args.heads
     heads = cfgd["heads"]
     if heads % world:
         raise SystemExit(f"{heads} heads do not shard over {world} GPUs")
@@ -276,6 +278,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
