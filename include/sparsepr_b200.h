@@ -154,6 +154,19 @@ int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_
 /* Scratch bytes needed by spr_block_sparse_attn. */
 size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq);
 
+/* ---------------------------------------------------------------- small linear algebra */
+
+/*
+ * Batched symmetric eigendecomposition (cyclic two-sided Jacobi, one CTA per
+ * matrix): a [batch,n,n] fp32 (symmetrised on load), n even <= 128.  Outputs
+ * evals [batch,n] ascending and evecs [batch,n,n] with eigenvectors in the
+ * columns, the torch.linalg.eigh convention.  Replaces the torch.linalg.eigh calls of
+ * src/sparsepr/models/cosmos3/operator_kmeans.py:94-151 (metric_factor) and
+ * src/sparsepr/models/cosmos3/residual_repair.py:468-491 (reduced_rank_output_basis).
+ */
+int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
+                void* stream);
+
 /* ---------------------------------------------------------------- repair */
 
 /*

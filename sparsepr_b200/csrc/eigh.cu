@@ -1,0 +1,142 @@
+// Batched symmetric eigendecomposition of small matrices (n <= 128, even),
+// one CTA per matrix, cyclic two-sided Jacobi with a round-robin pair
+// ordering (Golub & Van Loan, "Matrix Computations", sym.schur2 rotations and
+// the parallel-ordering cyclic Jacobi method).  Used for the role-metric
+// factors (128x128) and the repair basis (64x64 row Gram).
+//
+// Output matches torch.linalg.eigh's convention: eigenvalues ascending,
+// eigenvectors in the columns of a row-major [n][n] matrix.
+#include "common.cuh"
+
+namespace spr {
+
+constexpr int kEigMax = 128;
+constexpr int kEigLd = kEigMax + 1;  // padded row stride: column sweeps are bank-conflict free
+constexpr int kEigThreads = 512;
+
+__global__ void __launch_bounds__(kEigThreads)
+sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals, float* __restrict__ evecs,
+               int max_sweeps, float rel_tol) {
+  extern __shared__ float sh[];
+  float* A = sh;                        // [n][kEigLd]
+  float* V = sh + kEigMax * kEigLd;     // [n][kEigLd]
+  __shared__ float s_c[kEigMax / 2], s_s[kEigMax / 2];
+  __shared__ int s_p[kEigMax / 2], s_q[kEigMax / 2];
+  __shared__ int s_arr[kEigMax];
+  __shared__ float s_red[kEigThreads / 32][2];
+  __shared__ int s_stop;
+  const int64_t b = blockIdx.x;
+  const float* src = a_in + b * (int64_t)n * n;
+  const int tid = threadIdx.x;
+  for (int idx = tid; idx < n * n; idx += blockDim.x) {
+    const int i = idx / n, j = idx % n;
+    A[i * kEigLd + j] = 0.5f * (src[i * n + j] + src[j * n + i]);
+    V[i * kEigLd + j] = i == j ? 1.f : 0.f;
+  }
+  for (int i = tid; i < n; i += blockDim.x) s_arr[i] = i;
+  const int half = n / 2;
+  __syncthreads();
+  for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+    // Convergence test: off-diagonal mass relative to the total.
+    float off = 0.f, tot = 0.f;
+    for (int idx = tid; idx < n * n; idx += blockDim.x) {
+      const int i = idx / n, j = idx % n;
+      const float x = A[i * kEigLd + j];
+      tot += x * x;
+      if (i != j) off += x * x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      off += __shfl_xor_sync(0xffffffffu, off, o);
+      tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    }
+    if ((tid & 31) == 0) { s_red[tid >> 5][0] = off; s_red[tid >> 5][1] = tot; }
+    __syncthreads();
+    if (tid == 0) {
+      float so = 0.f, st = 0.f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { so += s_red[w][0]; st += s_red[w][1]; }
+      s_stop = so <= rel_tol * rel_tol * st;
+    }
+    __syncthreads();
+    if (s_stop) break;
+    for (int round = 0; round < n - 1; ++round) {
+      if (tid < half) {
+        int p = s_arr[tid], q = s_arr[n - 1 - tid];
+        if (p > q) { const int t = p; p = q; q = t; }
+        const float apq = A[p * kEigLd + q];
+        float c = 1.f, s = 0.f;
+        if (fabsf(apq) > 1e-30f) {
+          const float tau = (A[q * kEigLd + q] - A[p * kEigLd + p]) / (2.f * apq);
+          const float t = copysignf(1.f, tau) / (fabsf(tau) + sqrtf(1.f + tau * tau));
+          c = rsqrtf(1.f + t * t);
+          s = t * c;
+        }
+        s_p[tid] = p; s_q[tid] = q; s_c[tid] = c; s_s[tid] = s;
+      }
+      __syncthreads();
+      // Rows: A <- J^T A.
+      for (int idx = tid; idx < half * n; idx += blockDim.x) {
+        const int pr = idx / n, j = idx % n;
+        const int p = s_p[pr], q = s_q[pr];
+        const float c = s_c[pr], s = s_s[pr];
+        const float ap = A[p * kEigLd + j], aq = A[q * kEigLd + j];
+        A[p * kEigLd + j] = c * ap - s * aq;
+        A[q * kEigLd + j] = s * ap + c * aq;
+      }
+      __syncthreads();
+      // Columns: A <- A J, V <- V J.
+      for (int idx = tid; idx < half * n; idx += blockDim.x) {
+        const int pr = idx / n, i = idx % n;
+        const int p = s_p[pr], q = s_q[pr];
+        const float c = s_c[pr], s = s_s[pr];
+        const float ap = A[i * kEigLd + p], aq = A[i * kEigLd + q];
+        A[i * kEigLd + p] = c * ap - s * aq;
+        A[i * kEigLd + q] = s * ap + c * aq;
+        const float vp = V[i * kEigLd + p], vq = V[i * kEigLd + q];
+        V[i * kEigLd + p] = c * vp - s * vq;
+        V[i * kEigLd + q] = s * vp + c * vq;
+      }
+      __syncthreads();
+      if (tid == 0) {  // round-robin: keep slot 0, rotate the rest
+        const int last = s_arr[n - 1];
+        for (int i = n - 1; i > 1; --i) s_arr[i] = s_arr[i - 1];
+        s_arr[1] = last;
+      }
+      __syncthreads();
+    }
+  }
+  // Ascending order of the diagonal (ties by index), eigenvectors follow.
+  for (int j = tid; j < n; j += blockDim.x) {
+    const float lj = A[j * kEigLd + j];
+    int rank = 0;
+    for (int i = 0; i < n; ++i) {
+      const float li = A[i * kEigLd + i];
+      rank += (li < lj) || (li == lj && i < j);
+    }
+    evals[b * n + rank] = lj;
+    s_arr[j] = rank;
+  }
+  __syncthreads();
+  float* out = evecs + b * (int64_t)n * n;
+  for (int idx = tid; idx < n * n; idx += blockDim.x) {
+    const int i = idx / n, j = idx % n;
+    out[i * n + s_arr[j]] = V[i * kEigLd + j];
+  }
+}
+
+}  // namespace spr
+
+using namespace spr;
+
+extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
+                           void* stream) {
+  if (batch <= 0 || batch > 65535 || n < 2 || n > kEigMax || (n & 1))
+    return fail(SPR_ERR_SHAPE, "sym_eig: need 0 < batch <= 65535 and even 2 <= n <= 128, got batch=%lld n=%d",
+                (long long)batch, n);
+  if (max_sweeps < 1 || max_sweeps > 64) return fail(SPR_ERR_ARG, "sym_eig: max_sweeps=%d must be in [1,64]", max_sweeps);
+  const int smem = 2 * kEigMax * kEigLd * (int)sizeof(float);
+  cudaFuncSetAttribute(sym_eig_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  sym_eig_kernel<<<(unsigned)batch, kEigThreads, smem, (cudaStream_t)stream>>>(a, n, evals, evecs, max_sweeps,
+                                                                               1e-7f);
+  return check_launch("sym_eig");
+}

@@ -222,3 +222,18 @@ def repair_apply(base: torch.Tensor, state, alpha: float, rows: torch.Tensor | N
     _lib.call("spr_repair_apply", _p(_contig("base", base)), _p(x_mean), _p(x_scale), _p(y_mean), _p(left), _p(basis),
               b, n, d, r, float(alpha), _p(rows_i), _p(dense_b), m, _p(out), _stream(dev))
     return out
+
+
+def sym_eig(a: torch.Tensor, max_sweeps: int = 15):
+    """Batched symmetric eigendecomposition of [B,n,n] (n even <= 128):
+    (eigenvalues ascending [B,n], eigenvectors in columns [B,n,n]), fp32."""
+    dev = _cuda(a)
+    b, n, n2 = a.shape
+    if n != n2:
+        raise RuntimeError(f"sym_eig expects square matrices, got {tuple(a.shape)}")
+    a = a.to(torch.float32).contiguous()
+    evals = torch.empty((b, n), dtype=torch.float32, device=dev)
+    evecs = torch.empty((b, n, n), dtype=torch.float32, device=dev)
+    _count(1)
+    _lib.call("spr_sym_eig", _p(a), b, n, int(max_sweeps), _p(evals), _p(evecs), _stream(dev))
+    return evals, evecs

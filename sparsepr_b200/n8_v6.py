@@ -200,9 +200,7 @@ def metric_factor(metric: torch.Tensor, rank: int) -> torch.Tensor:
         raise RuntimeError(f"Expected batched square metrics, got {tuple(metric.shape)}.")
     if rank <= 0 or rank > metric.shape[-1]:
         raise RuntimeError(f"rank must be in [1, {metric.shape[-1]}], got {rank}.")
-    m = metric.float()
-    m = 0.5 * (m + m.transpose(1, 2))
-    evals, evecs = torch.linalg.eigh(m)
+    evals, evecs = K.sym_eig(metric.float())  # symmetrised inside the kernel
     evals = evals[:, -rank:].clamp_min(0.0)
     evecs = evecs[:, :, -rank:]
     norm = evals.mean(dim=1, keepdim=True).clamp_min(1e-12)
@@ -307,7 +305,7 @@ def fit_reduced_rank_residual(x_fit, y_fit, weights, rank: int, ridge: float):
     gram.diagonal(dim1=1, dim2=2).add_(float(ridge))
     chol, _info = torch.linalg.cholesky_ex(gram, check_errors=False)
     dual = torch.cholesky_solve(yw, chol)
-    evals, evecs = torch.linalg.eigh(torch.bmm(yw, yw.transpose(1, 2)))
+    evals, evecs = K.sym_eig(torch.bmm(yw, yw.transpose(1, 2)))
     evecs = evecs[:, :, -rank:]
     scales = evals[:, -rank:].clamp_min(1e-20).rsqrt().unsqueeze(1)
     basis = (torch.bmm(yw.transpose(1, 2), evecs) * scales).contiguous()

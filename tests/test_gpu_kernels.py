@@ -146,3 +146,23 @@ def test_selector_matches_oracle_bit_exact(cuda, ck):
     rid, rcnt = oracle.compact_selected(ref[:, 1:, 1:])
     assert torch.equal(counts.cpu(), rcnt)
     assert torch.equal(ids.cpu(), rid)
+
+
+@pytest.mark.parametrize("n", [64, 128, 48, 2])
+def test_sym_eig_matches_lapack(cuda, n):
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(5, 3 * n + 7, n, generator=g)
+    a = x.transpose(1, 2) @ x / x.shape[1]
+    a[1] = a[1] * 0  # all-zero matrix
+    a[2, :, :] = torch.diag(torch.arange(n, 0, -1).float())  # already diagonal, descending
+    w, v = K.sym_eig(a.to(cuda))
+    w, v = w.cpu().double(), v.cpu().double()
+    wr = torch.linalg.eigvalsh(a.double())
+    scale = wr.abs().amax(dim=1, keepdim=True).clamp_min(1.0)
+    assert ((w - wr).abs() / scale).max().item() < 1e-5
+    ad = a.double()
+    resid = (ad @ v - v * w.unsqueeze(1)).abs().amax(dim=(1, 2)) / scale.squeeze(1)
+    assert resid.max().item() < 1e-4
+    eye = torch.eye(n, dtype=torch.float64)
+    assert (v.transpose(1, 2) @ v - eye).abs().max().item() < 1e-4
+    assert torch.all(w[:, 1:] >= w[:, :-1])
