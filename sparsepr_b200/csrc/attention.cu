@@ -1,96 +1,78 @@
-// Block-sparse flash attention over kept (query-cluster, key-cluster) pairs.
+// Block-sparse flash attention over kept (query-cluster, key-cluster) pairs on
+// the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// Work unit: one 64-row tile of one query cluster (rows of the cluster-sorted
-// Q).  Its keys are the concatenated token runs of the selected key clusters
-// of the cluster-sorted K/V; 64-key tiles are gathered row by row with
-// 16-byte cp.async (no index list is materialised), double buffered.
-// bf16 tensor-core MMA with fp32 accumulation and an online softmax; the
-// output row is stored through the inverse permutation when q_order is given.
-#include "common.cuh"
+// Work unit (one CTA): a 128-row tile of one query cluster of the
+// cluster-sorted Q.  Its keys are the concatenated token runs of the selected
+// key clusters of the cluster-sorted K/V, consumed in 128-key tiles; only the
+// last tile of a cluster can be partial, so masking is a column bound.
+//
+// Warp roles (256 threads):
+//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t).  Loads the
+//              S row from TMEM, online softmax in base 2 with a lazily
+//              updated running max, writes P (bf16) to shared memory, rescales
+//              the O accumulator in TMEM when the max moves, and finally
+//              normalises O and stores the row (through q_order: the inverse
+//              permute is fused into the store).
+//   warp 4     MMA issuer (one thread): S(j) = Q K_j^T into one of two TMEM S
+//              buffers, O += P(j) V_j into the TMEM O accumulator.
+//   warps 5-7  loaders: gather the K/V rows of each key tile with 16-byte
+//              cp.async into a 2-stage ring (no index list is materialised).
+// TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O.
+// Operand tiles use the canonical 128-byte-swizzled K-major layout; V is the
+// MN-major B operand of the PV product.
+#include "tc_common.cuh"
 
 namespace spr {
 
-constexpr int kD = 128;       // head dim
-constexpr int kBM = 64;       // query rows per CTA (16 per warp)
-constexpr int kBN = 64;       // keys per tile
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kChunks = kD * 2 / 16;  // 16-byte chunks per row (16)
+using namespace tc;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+constexpr int kD = 128;
+constexpr int kTileM = 128;
+constexpr int kTileN = 128;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kLoaderThreads = 96;
+constexpr int kThreadsTc = 256;
+constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
+constexpr int kSmemTc = 1024 /*align slack*/ + kTileBytes /*Q*/ + 4 * kTileBytes /*K,V x2*/ + kTileBytes /*P*/;
+constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 1);
 
-// Swizzled byte offset of (row, 16-byte chunk) in a [rows][128] bf16 tile.
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return (uint32_t)(row * (kD * 2) + ((chunk ^ (row & 7)) << 4));
-}
+enum : int { kErrTimeoutLoad = 1, kErrTimeoutMma = 2, kErrTimeoutSoftmax = 3 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(n));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// tile_start[b][c] = first 64-row tile of query cluster c in problem b
-// (exclusive prefix of ceil(size/64)); tile_start[b][cq] = tiles of b.
-__global__ void tile_table_kernel(const int32_t* __restrict__ q_offsets, int cq, int32_t* __restrict__ tile_start) {
+// err[0] = 0, tile_start[b][c] = first 128-row tile of query cluster c in
+// problem b (exclusive prefix of ceil(size/128)); tile_start[b][cq] = total.
+__global__ void tile_table_kernel(const int32_t* __restrict__ q_offsets, int cq, int32_t* __restrict__ tile_start,
+                                  int* __restrict__ err) {
   const int64_t b = blockIdx.x;
   if (threadIdx.x != 0) return;
+  if (b == 0) *err = 0;
   int32_t acc = 0;
   for (int c = 0; c < cq; ++c) {
     tile_start[b * (cq + 1) + c] = acc;
     const int32_t sz = q_offsets[b * (cq + 1) + c + 1] - q_offsets[b * (cq + 1) + c];
-    acc += (sz + kBM - 1) / kBM;
+    acc += (sz + kTileM - 1) / kTileM;
   }
   tile_start[b * (cq + 1) + cq] = acc;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-block_sparse_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                         const __nv_bfloat16* __restrict__ v, const int32_t* __restrict__ q_offsets,
-                         const int32_t* __restrict__ k_offsets, const int32_t* __restrict__ sel_ids,
-                         const int32_t* __restrict__ sel_counts, const int32_t* __restrict__ tile_start,
-                         int64_t nq, int64_t nk, int cq, int ck, const int32_t* __restrict__ q_order,
-                         __nv_bfloat16* __restrict__ out, float scale_log2) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sQ = smem;                          // 64 x 128
-  uint8_t* sK = smem + kBM * kD * 2;           // 2 x 64 x 128
-  uint8_t* sV = sK + 2 * kBN * kD * 2;         // 2 x 64 x 128
-  __shared__ int32_t s_src[2][kBN];
-  __shared__ int s_ntiles;
+__global__ void __launch_bounds__(kThreadsTc, 1)
+block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                            const __nv_bfloat16* __restrict__ v, const int32_t* __restrict__ q_offsets,
+                            const int32_t* __restrict__ k_offsets, const int32_t* __restrict__ sel_ids,
+                            const int32_t* __restrict__ sel_counts, const int32_t* __restrict__ tile_start,
+                            int64_t nq, int64_t nk, int cq, int ck, const int32_t* __restrict__ q_order,
+                            __nv_bfloat16* __restrict__ out, float scale_log2, int* __restrict__ err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_kv_full[2], bar_kv_empty[2], bar_s_full[2], bar_p_full, bar_o_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int32_t s_src[2][kTileN];
+  __shared__ int s_total;
 
   const int64_t b = blockIdx.y;
   const int tile = blockIdx.x;
   const int32_t* ts = tile_start + b * (cq + 1);
-  if (tile >= ts[cq]) return;
-  // Query cluster owning this tile: the last c with ts[c] <= tile.
-  int lo = 0, hi = cq - 1;
+  if (tile >= ts[cq]) return;  // block-uniform, before any barrier or TMEM use
+  int lo = 0, hi = cq - 1;     // query cluster owning the tile: last c with ts[c] <= tile
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (ts[mid] <= tile) lo = mid; else hi = mid - 1;
@@ -98,8 +80,14 @@ block_sparse_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
   const int c = lo;
   const int32_t qbeg = q_offsets[b * (cq + 1) + c];
   const int32_t qend = q_offsets[b * (cq + 1) + c + 1];
-  const int32_t row0 = qbeg + (tile - ts[c]) * kBM;
-  const int rows = min(kBM, qend - row0);
+  const int32_t row0 = qbeg + (tile - ts[c]) * kTileM;
+  const int rows = min(kTileM, qend - row0);
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;        // 2 stages
+  uint8_t* sV = sK + 2 * kTileBytes;    // 2 stages
+  uint8_t* sP = sV + 2 * kTileBytes;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* qb = q + b * nq * kD;
@@ -109,179 +97,221 @@ block_sparse_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat1
   const int nsel = sel_counts[b * cq + c];
   const int32_t* ko = k_offsets + b * (ck + 1);
 
-  // Q tile.
-  for (int i = tid; i < kBM * kChunks; i += kThreads) {
-    const int r = i / kChunks, ch = i % kChunks;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_kv_full[i], kLoaderThreads);
+      mbar_init(&bar_kv_empty[i], 1);
+      mbar_init(&bar_s_full[i], 1);
+    }
+    mbar_init(&bar_p_full, kSoftmaxThreads);
+    mbar_init(&bar_o_done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 4) tmem_alloc<512>(&s_tmem);
+  if (warp == 5) {  // total selected keys of this query cluster
+    int64_t t = 0;
+    for (int i = lane; i < nsel; i += 32) {
+      const int kc = ids[i];
+      t += ko[kc + 1] - ko[kc];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) s_total = (int)t;
+  }
+  // Q tile (all threads), zero rows past the cluster end.
+  for (int i = tid; i < kTileM * 16; i += kThreadsTc) {
+    const int r = i >> 4, ch = i & 15;
     const bool ok = r < rows;
-    cp_async16(smem_u32(sQ + swz(r, ch)), qb + (int64_t)(row0 + (ok ? r : 0)) * kD + ch * 8, ok);
+    cp_async16(smem_addr(sQ) + sw128_off(r, ch, kTileM), qb + (int64_t)(row0 + (ok ? r : 0)) * kD + ch * 8, ok);
   }
   cp_async_commit();
-
-  // Thread 0 walks the selected runs and publishes each key tile's slot map.
-  int cur_pos = 0, cur_off = 0;
-  auto build_tile = [&](int buf) {
-    int filled = 0;
-    while (filled < kBN && cur_pos < nsel) {
-      const int kc = ids[cur_pos];
-      const int32_t rb = ko[kc], re = ko[kc + 1];
-      const int32_t avail = (re - rb) - cur_off;
-      if (avail <= 0) { cur_pos++; cur_off = 0; continue; }
-      const int take = min(avail, kBN - filled);
-      for (int j = 0; j < take; ++j) s_src[buf][filled + j] = rb + cur_off + j;
-      filled += take;
-      cur_off += take;
-    }
-    for (int j = filled; j < kBN; ++j) s_src[buf][j] = -1;
-  };
-  auto issue_kv = [&](int buf) {
-    for (int i = tid; i < kBN * kChunks; i += kThreads) {
-      const int r = i / kChunks, ch = i % kChunks;
-      const int32_t src = s_src[buf][r];
-      const bool ok = src >= 0;
-      const int64_t off = (int64_t)(ok ? src : 0) * kD + ch * 8;
-      cp_async16(smem_u32(sK + buf * kBN * kD * 2 + swz(r, ch)), kb + off, ok);
-      cp_async16(smem_u32(sV + buf * kBN * kD * 2 + swz(r, ch)), vb + off, ok);
-    }
-    cp_async_commit();
-  };
-
-  if (tid == 0) {
-    int64_t tot = 0;
-    for (int i = 0; i < nsel; ++i) tot += ko[ids[i] + 1] - ko[ids[i]];
-    s_ntiles = (int)((tot + kBN - 1) / kBN);
-    build_tile(0);
-  }
+  cp_async_wait_all();
+  fence_proxy_async_smem();
+  tc_fence_before();
   __syncthreads();
-  const int ntiles = s_ntiles;
-  if (ntiles > 0) issue_kv(0);
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int total = s_total;
+  const int ntiles = (total + kTileN - 1) / kTileN;
 
-  float o[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-  uint32_t qa[8][4];  // Q fragments for this warp's 16 rows, 8 k-steps of 16
-  const int t4 = lane & 3;
-
-  for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) {
-      if (tid == 0) build_tile(buf ^ 1);
-      __syncthreads();
-      issue_kv(buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+  if (warp >= 5) {
+    // ------------------------------------------------------------ loaders
+    const int lt = tid - 5 * 32;
+    int cur_pos = 0, cur_off = 0;  // run cursor, meaningful in lt == 0
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      if (lt == 0) {
+        bool ok = true;
+        if (j >= 2) ok = mbar_wait(&bar_kv_empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
+        int filled = 0;
+        while (ok && filled < kTileN && cur_pos < nsel) {
+          const int kc = ids[cur_pos];
+          const int32_t rb = ko[kc], re = ko[kc + 1];
+          const int32_t avail = (re - rb) - cur_off;
+          if (avail <= 0) { ++cur_pos; cur_off = 0; continue; }
+          const int take = min(avail, kTileN - filled);
+          for (int x = 0; x < take; ++x) s_src[st][filled + x] = rb + cur_off + x;
+          filled += take;
+          cur_off += take;
+        }
+        for (int x = filled; x < kTileN; ++x) s_src[st][x] = -1;
+      }
+      named_bar(1, kLoaderThreads);
+      const uint32_t dk = smem_addr(sK + st * kTileBytes), dv = smem_addr(sV + st * kTileBytes);
+      for (int i = lt; i < kTileN * 16; i += kLoaderThreads) {
+        const int r = i >> 4, ch = i & 15;
+        const int32_t src = s_src[st][r];
+        const bool ok = src >= 0;
+        const int64_t off = (int64_t)(ok ? src : 0) * kD + ch * 8;
+        const uint32_t o = sw128_off(r, ch, kTileN);
+        cp_async16(dk + o, kb + off, ok);
+        cp_async16(dv + o, vb + off, ok);
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      mbar_arrive(&bar_kv_full[st]);
     }
-    __syncthreads();
-    if (t == 0) {
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t tS[2] = {tmem, tmem + 128};
+      const uint32_t tO = tmem + 256;
+      const uint32_t aq = smem_addr(sQ), ap = smem_addr(sP);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&bar_kv_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t bk = smem_addr(sK + st * kTileBytes);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int r = warp * 16 + (lane & 15);
-        const int ch = kk * 2 + (lane >> 4);
-        ldsm_x4(smem_u32(sQ + swz(r, ch)), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+        for (int kk = 0; kk < kD / 16; ++kk) {  // K-major: 32 B per 16-element step, second half +16 KB
+          const uint32_t koff = (kk >> 2) * (kTileM * 128) + (kk & 3) * 32;
+          mma_f16(tS[st], sw128_desc(aq + koff, 16, 1024), sw128_desc(bk + koff, 16, 1024), kIdescQK, kk > 0);
+        }
+        mma_commit(&bar_s_full[st]);
+        return true;
+      };
+      bool ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j & 1;
+        if (!(ok = mbar_wait(&bar_p_full, j & 1, err, kErrTimeoutMma))) break;
+        tc_fence_after();
+        const uint32_t bv = smem_addr(sV + st * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kTileN / 16; ++kk) {  // 16 keys per step
+          const uint32_t poff = (kk >> 2) * (kTileM * 128) + (kk & 3) * 32;  // P is K-major over keys
+          const uint32_t voff = kk * 2048;                                   // V is MN-major: 16 rows = 2 x 1024 B
+          mma_f16(tO, sw128_desc(ap + poff, 16, 1024), sw128_desc(bv + voff, kTileN * 128, 1024), kIdescPV,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&bar_o_done);
+        mma_commit(&bar_kv_empty[st]);
+        if (j + 2 < ntiles) ok = issue_s(j + 2);
       }
     }
-    const uint8_t* tK = sK + buf * kBN * kD * 2;
-    const uint8_t* tV = sV + buf * kBN * kD * 2;
-    // S = Q K^T for 16 rows x 64 keys.
-    float s[8][4];
+  } else {
+    // ------------------------------------------------------------ softmax (thread = row)
+    const int row = tid;  // TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s_full[st], (j >> 1) & 1, err, kErrTimeoutSoftmax));
+      if (!ok) break;
+      tc_fence_after();
+      float s[kTileN];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+      for (int cb = 0; cb < 4; ++cb) tmem_ld32(tmem + lane_base + st * 128 + cb * 32, s + cb * 32);
+      const int valid = min(kTileN, total - j * kTileN);
+      float mx = -INFINITY;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+      for (int x = 0; x < kTileN; ++x) {
+        s[x] = x < valid ? s[x] * scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[x]);
+      }
+      // Lazy max: keep the running max unless it grew by more than 8 (base 2).
+      float alpha = 1.f;
+      if (mx > m_run + 8.f || m_run == -INFINITY) {
+        alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
+        m_run = mx;
+      }
+      float sum = 0.f;
+      uint32_t pk[kTileN / 2];
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {  // pairs of 8-key n tiles
-        const int r = np * 16 + ((lane >> 4) << 3) + (lane & 7);
-        const int ch = kk * 2 + ((lane >> 3) & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(tK + swz(r, ch)), b0, b1, b2, b3);
-        mma_bf16(s[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
-        mma_bf16(s[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+      for (int x = 0; x < kTileN; x += 2) {
+        const float p0 = exp2f(s[x] - m_run), p1 = exp2f(s[x + 1] - m_run);
+        sum += p0 + p1;
+        __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+        pk[x >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      l_run = l_run * alpha + sum;
+      if (j > 0) {
+        // PV(j-1) must be complete before O is rescaled and P is overwritten.
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_o_done, (j - 1) & 1, err, kErrTimeoutSoftmax));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // warp-uniform: TMEM ld/st are warp-collective
+          float o[32];
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) {
+            tmem_ld32(tmem + lane_base + 256 + cb * 32, o);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) o[x] *= alpha;
+            tmem_st32(tmem + lane_base + 256 + cb * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      const uint32_t pbase = smem_addr(sP);
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const uint32_t a = pbase + sw128_off(row, ch, kTileM);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(pk[ch * 4]), "r"(pk[ch * 4 + 1]),
+                     "r"(pk[ch * 4 + 2]), "r"(pk[ch * 4 + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_p_full);
+    }
+    // Epilogue: O / l, bf16, stored through the inverse permutation.
+    if (ok && ntiles > 0) ok = mbar_wait(&bar_o_done, (ntiles - 1) & 1, err, kErrTimeoutSoftmax);
+    const bool have = __all_sync(0xffffffffu, ok && ntiles > 0);
+    tc_fence_after();
+    const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
+    const int64_t s_row = row0 + row;
+    const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
+    uint4* orow = reinterpret_cast<uint4*>(out + (b * nq + dst) * kD);
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      float o[32];
+      if (have) {
+        tmem_ld32(tmem + lane_base + 256 + cb * 32, o);
+      } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) o[x] = 0.f;
+      }
+      if (row < rows) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
+            w[e] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          orow[cb * 4 + q4] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
     }
-    // Mask invalid key slots, online softmax (base 2).
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = j * 8 + 2 * t4 + (e & 1);
-        float val = s[j][e] * scale_log2;
-        if (s_src[buf][key] < 0) val = -INFINITY;
-        s[j][e] = val;
-        mx[e >> 1] = fmaxf(mx[e >> 1], val);
-      }
-    }
-    float alpha[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-      const float mn = fmaxf(m_r[h], mx[h]);
-      alpha[h] = (m_r[h] == -INFINITY) ? 0.f : exp2f(m_r[h] - mn);
-      m_r[h] = mn;
-    }
-    float rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float mref = m_r[e >> 1];
-        const float p = (mref == -INFINITY) ? 0.f : exp2f(s[j][e] - mref);
-        s[j][e] = p;
-        rs[e >> 1] += p;
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) l_r[h] = l_r[h] * alpha[h] + rs[h];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= alpha[0]; o[j][1] *= alpha[0];
-      o[j][2] *= alpha[1]; o[j][3] *= alpha[1];
-    }
-    // O += P V.
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {  // 16 keys per step
-      const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int np = 0; np < 8; ++np) {  // pairs of 8-wide d tiles
-        const int r = kk * 16 + (((lane >> 3) & 1) << 3) + (lane & 7);
-        const int ch = np * 2 + (lane >> 4);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(tV + swz(r, ch)), b0, b1, b2, b3);
-        mma_bf16(o[2 * np], a0, a1, a2, a3, b0, b1);
-        mma_bf16(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
-      }
-    }
-    __syncthreads();  // buffer `buf` is refilled in the next iteration
   }
-
-  cp_async_wait<0>();  // the Q group is still pending when the cluster has no keys
-  float inv[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float l = l_r[h];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    inv[h] = l > 0.f ? 1.f / l : 0.f;
-  }
-  const int g = lane >> 2;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int r = warp * 16 + g + h * 8;
-    if (r >= rows) continue;
-    const int64_t s_row = row0 + r;
-    const int64_t dst = q_order ? (int64_t)q_order[b * nq + s_row] : s_row;
-    __nv_bfloat16* orow = out + (b * nq + dst) * kD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = j * 8 + 2 * t4;
-      *reinterpret_cast<__nv_bfloat162*>(orow + col) =
-          __floats2bfloat162_rn(o[j][2 * h] * inv[h], o[j][2 * h + 1] * inv[h]);
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
   }
 }
 
@@ -291,7 +321,7 @@ using namespace spr;
 
 extern "C" size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq) {
   (void)nq;
-  return align_up((size_t)bh * (cq + 1) * sizeof(int32_t), 256) + 256;
+  return 256 + align_up((size_t)bh * (cq + 1) * sizeof(int32_t), 256) + 256;
 }
 
 extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_perm,
@@ -305,21 +335,21 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
   if (!aligned(q_perm, 16) || !aligned(k_perm, 16) || !aligned(v_perm, 16) || !aligned(out, 16))
     return fail(SPR_ERR_ALIGN, "block-sparse attention: 16-byte alignment required");
   Carver cv(workspace, workspace_bytes);
+  int* err = cv.take<int>(64);
   int32_t* tile_start = cv.take<int32_t>((size_t)bh * (cq + 1));
   if (!workspace || !cv.ok())
     return fail(SPR_ERR_WORKSPACE, "block-sparse attention: workspace %zu < %zu", workspace_bytes, cv.off);
   cudaStream_t st = (cudaStream_t)stream;
-  tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start);
+  tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   int s = check_launch("attention tile table");
   if (s) return s;
-  const int smem = (kBM + 4 * kBN) * kD * 2;
-  cudaFuncSetAttribute(block_sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
   // Upper bound on tiles per problem: every cluster may add one partial tile.
-  const int64_t max_tiles = (nq + kBM - 1) / kBM + cq;
+  const int64_t max_tiles = (nq + kTileM - 1) / kTileM + cq;
   dim3 grid((unsigned)max_tiles, (unsigned)bh);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
-  block_sparse_attn_kernel<<<grid, kThreads, smem, st>>>(
+  block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
       (const __nv_bfloat16*)q_perm, (const __nv_bfloat16*)k_perm, (const __nv_bfloat16*)v_perm, q_offsets, k_offsets,
-      sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2);
+      sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
   return check_launch("block-sparse attention");
 }

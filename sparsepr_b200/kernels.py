@@ -194,6 +194,16 @@ def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids
     return out
 
 
+def attention_error_code(dev: torch.device) -> int:
+    """Device status word of the last block-sparse attention launch on ``dev``
+    (0 = ok, else the bounded wait that gave up).  Synchronises; for tests."""
+    ws = _WS.get((dev.type, dev.index, "attn"))
+    if ws is None:
+        return 0
+    torch.cuda.synchronize(dev)
+    return int(ws[:4].view(torch.int32).item())
+
+
 def dense_attention_rows(q_rows: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """Exact attention of [B,M,D] query rows against all [B,N,D] keys (one cluster pair)."""
     dev = _cuda(q_rows, k, v)

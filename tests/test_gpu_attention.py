@@ -53,6 +53,7 @@ def test_block_sparse_attention_matches_oracle(cuda, n, cq, ck, density):
     ids, cnt = oracle.compact_selected(mask)
     got = K.block_sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), _i32(oracle.cluster_offsets(qs), cuda),
                                    _i32(oracle.cluster_offsets(ks), cuda), _i32(ids, cuda), _i32(cnt, cuda))
+    assert K.attention_error_code(cuda) == 0
     _close(got, ref)
     qo = oracle.cluster_offsets(qs)
     for h in range(bh):  # key-less cluster -> zeros
