@@ -31,17 +31,20 @@ __global__ void permute_rows_kernel(const uint4* __restrict__ x, const int32_t* 
   }
 }
 
-// Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym)); one warp per row.
+// Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym)); one warp per
+// row, lane l owns dims l, l+32, l+64, l+96 (L and B are staged transposed so
+// the shared-memory reads are conflict free).
 template <int D, int R>
 __global__ void __launch_bounds__(256)
 repair_apply_kernel(const __nv_bfloat16* __restrict__ base, const float* __restrict__ xm,
                     const float* __restrict__ xs, const float* __restrict__ ym, const float* __restrict__ left,
                     const float* __restrict__ basis, int64_t n, float alpha, __nv_bfloat16* __restrict__ out) {
-  __shared__ float sh_l[D * R], sh_b[D * R], sh_xm[D], sh_xs[D], sh_ym[D];
+  __shared__ float sh_lt[R * D], sh_bt[R * D], sh_xm[D], sh_xs[D], sh_ym[D];
   const int64_t b = blockIdx.y;
   for (int i = threadIdx.x; i < D * R; i += blockDim.x) {
-    sh_l[i] = left[b * D * R + i];
-    sh_b[i] = basis[b * D * R + i];
+    const int dd = i / R, j = i % R;
+    sh_lt[j * D + dd] = left[b * D * R + i];
+    sh_bt[j * D + dd] = basis[b * D * R + i];
   }
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     sh_xm[i] = xm[b * D + i];
@@ -49,16 +52,16 @@ repair_apply_kernel(const __nv_bfloat16* __restrict__ base, const float* __restr
     sh_ym[i] = ym[b * D + i];
   }
   __syncthreads();
-  constexpr int PER = D / 32;  // dims per lane (contiguous)
+  constexpr int PER = D / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rows_per_block = blockDim.x >> 5;
   for (int64_t r = (int64_t)blockIdx.x * rows_per_block + warp; r < n; r += (int64_t)gridDim.x * rows_per_block) {
-    const __nv_bfloat16* br = base + (b * n + r) * D + lane * PER;
+    const __nv_bfloat16* br = base + (b * n + r) * D;
     float v[PER], z[PER];
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
-      v[e] = __bfloat162float(br[e]);
-      const int dd = lane * PER + e;
+      const int dd = lane + 32 * e;
+      v[e] = __bfloat162float(br[dd]);
       z[e] = (v[e] - sh_xm[dd]) / sh_xs[dd];
     }
     float coord[R];
@@ -66,19 +69,19 @@ repair_apply_kernel(const __nv_bfloat16* __restrict__ base, const float* __restr
     for (int j = 0; j < R; ++j) {
       float p = 0.f;
 #pragma unroll
-      for (int e = 0; e < PER; ++e) p = fmaf(z[e], sh_l[(lane * PER + e) * R + j], p);
+      for (int e = 0; e < PER; ++e) p = fmaf(z[e], sh_lt[j * D + lane + 32 * e], p);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
       coord[j] = p;
     }
-    __nv_bfloat16* orow = out + (b * n + r) * D + lane * PER;
+    __nv_bfloat16* orow = out + (b * n + r) * D;
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
-      const int dd = lane * PER + e;
+      const int dd = lane + 32 * e;
       float c = sh_ym[dd];
 #pragma unroll
-      for (int j = 0; j < R; ++j) c = fmaf(coord[j], sh_b[dd * R + j], c);
-      orow[e] = __float2bfloat16(v[e] + alpha * c);
+      for (int j = 0; j < R; ++j) c = fmaf(coord[j], sh_bt[j * D + dd], c);
+      orow[dd] = __float2bfloat16(v[e] + alpha * c);
     }
   }
 }
@@ -118,7 +121,9 @@ extern "C" int spr_repair_apply(const void* base, const float* x_mean, const flo
   if (d != 128 || r != 16) return fail(SPR_ERR_SHAPE, "repair apply: requires d=128, r=16 (got d=%d r=%d)", d, r);
   if (bh <= 0 || n <= 0 || bh > 65535) return fail(SPR_ERR_SHAPE, "repair apply: bad shape");
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid((unsigned)std::min<int64_t>((n + 7) / 8, 4096), (unsigned)bh);
+  // A few hundred rows per block amortise the per-block load of the 16 KB repair state.
+  const int64_t per_head = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (148 * 8 + bh - 1) / bh));
+  dim3 grid((unsigned)per_head, (unsigned)bh);
   repair_apply_kernel<128, 16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)base, x_mean, x_scale, y_mean, left, basis,
                                                      n, alpha, (__nv_bfloat16*)out);
   int s = check_launch("repair apply");

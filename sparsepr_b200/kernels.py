@@ -209,8 +209,9 @@ def dense_attention_rows(q_rows: torch.Tensor, k: torch.Tensor, v: torch.Tensor)
     dev = _cuda(q_rows, k, v)
     b, m, _ = q_rows.shape
     n = k.shape[1]
-    q_off = torch.tensor([0, m], dtype=torch.int32, device=dev).expand(b, 2).contiguous()
-    k_off = torch.tensor([0, n], dtype=torch.int32, device=dev).expand(b, 2).contiguous()
+    two = torch.arange(2, dtype=torch.int32, device=dev)  # device-side: no host copy
+    q_off = (two * m).expand(b, 2).contiguous()
+    k_off = (two * n).expand(b, 2).contiguous()
     ids = torch.zeros((b, 1, 1), dtype=torch.int32, device=dev)
     cnt = torch.ones((b, 1), dtype=torch.int32, device=dev)
     return block_sparse_attention(q_rows.contiguous(), k, v, q_off, k_off, ids, cnt)

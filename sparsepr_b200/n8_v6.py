@@ -170,12 +170,31 @@ class N8V6Route:
 # Small per-head linear algebra (PyTorch / cuSOLVER on the device)
 # ----------------------------------------------------------------------------
 
+_DEVICE_CONST: dict[tuple, torch.Tensor] = {}
+
+
+def _device_const(key: tuple, make) -> torch.Tensor:
+    """Small constant index tensors built once on the host and cached per device,
+    so a route call never issues a blocking host-to-device copy."""
+    t = _DEVICE_CONST.get(key)
+    if t is None:
+        t = make()
+        _DEVICE_CONST[key] = t
+    return t
+
+
 def _sample_positions(tokens: int, sample_tokens: int, device) -> torch.Tensor | None:
     """Evenly spaced token positions (``operator_kmeans.py:52-59``)."""
     if sample_tokens <= 0 or sample_tokens >= tokens:
         return None
-    pos = torch.linspace(0, tokens - 1, steps=sample_tokens, device=device)
-    return pos.round().long().unique(sorted=True)
+    return _device_const(
+        ("sample", tokens, sample_tokens, str(device)),
+        lambda: torch.linspace(0, tokens - 1, steps=sample_tokens).round().long().unique(sorted=True).to(device))
+
+
+def _init_indices(bh: int, tokens: int, k: int, seed: int, device) -> torch.Tensor:
+    return _device_const(("init", bh, tokens, k, seed, str(device)),
+                         lambda: random_init_indices(bh, tokens, k, seed).to(device))
 
 
 def key_metric_from_queries(q: torch.Tensor, sample_tokens: int) -> torch.Tensor:
@@ -431,7 +450,7 @@ class N8V6Core:
             if k_init_features is None and warm:
                 k_init_features = torch.bmm(self.k_centroids, k_factor) / k_scale
         if k_init_features is None:
-            idx = random_init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed).to(dev)
+            idx = _init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev)
             k_init_features = torch.gather(k_feat, 1, idx.unsqueeze(-1).expand(-1, -1, k_feat.shape[-1]))
         k_labels, _kc, k_sizes, k_off, k_order, k_it = K.kmeans_lloyd(k_feat, k_init_features, iters, cfg.kmeans_tol)
 
@@ -465,7 +484,7 @@ class N8V6Core:
                 qi = torch.bmm(self.q_centroids, q_factor)
                 q_init_features = qi / qi.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)
         if q_init_features is None:
-            idx = random_init_indices(bh, tokens, cfg.num_q_centroids, cfg.kmeans_init_seed + 1).to(dev)
+            idx = _init_indices(bh, tokens, cfg.num_q_centroids, cfg.kmeans_init_seed + 1, dev)
             q_init_features = torch.gather(q_feat, 1, idx.unsqueeze(-1).expand(-1, -1, q_feat.shape[-1]))
         q_labels, _qc, q_sizes, q_off, q_order, q_it = K.kmeans_lloyd(q_feat, q_init_features, iters, cfg.kmeans_tol)
         q_cent, q_perm = K.centroid_means(q, q_order, q_off, cfg.num_q_centroids, self.q_centroids, permute=True)
