@@ -39,6 +39,11 @@ enum {
 /* Element type codes for `*_dtype` arguments. */
 enum { SPR_F32 = 0, SPR_BF16 = 1, SPR_F16 = 2 };
 
+/* Distance precision of the k-means assignment GEMM: TF32 tensor-core dot
+ * products (the reference's GPU behaviour), or 3xTF32 split products that
+ * reproduce fp32 dot products (d <= 64). */
+enum { SPR_KMEANS_TF32 = 0, SPR_KMEANS_FP32 = 1 };
+
 /* Library version (major*10000 + minor*100 + patch). */
 int spr_version(void);
 /* Message of the last failed call on this host thread ("" if none). */
@@ -46,7 +51,9 @@ const char* spr_last_error(void);
 
 /* ---------------------------------------------------------------- k-means */
 
-/* Scratch bytes needed by spr_kmeans_lloyd / spr_label_sort for a problem. */
+/* Scratch bytes needed by spr_kmeans_lloyd / spr_kmeans_assign / spr_label_sort.
+ * The first int32 of the workspace holds the device status of the last call
+ * (0 = ok, else a bounded wait inside a kernel gave up). */
 size_t spr_kmeans_workspace_bytes(int64_t bh, int64_t n, int d, int k);
 
 /*
@@ -58,13 +65,14 @@ size_t spr_kmeans_workspace_bytes(int64_t bh, int64_t n, int d, int k);
  * ids sorted by label, ties by token id), iters_done [1] i32.
  * centroid_round_dtype: SPR_F32, or x_dtype to round updated centroids to the
  * storage type each iteration like the standalone flash_kmeans path.
+ * precision: SPR_KMEANS_TF32 or SPR_KMEANS_FP32 (see above).
  * Replaces: src/sparsepr/kmeans_utils.py:1504-1580 batch_kmeans_Euclid(backend="flash")
  *   -> 1281-1465 (assign kmeans_utils.py:775-893 / flash_kmeans/assign_euclid_triton.py:803-1412,
  *   update flash_kmeans/centroid_update_triton.py:316-386, sizes kmeans_utils.py:1110-1157),
  *   and flash_kmeans/kmeans_triton_impl.py:55-115.
  */
 int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
-                     int iters, float tol, int centroid_round_dtype,
+                     int iters, float tol, int centroid_round_dtype, int precision,
                      float* centroids_inout, int32_t* labels, int32_t* sizes,
                      int32_t* offsets, int32_t* order, int32_t* iters_done,
                      void* workspace, size_t workspace_bytes, void* stream);
@@ -75,7 +83,8 @@ int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t n, int d, i
  * euclid_assign_triton.
  */
 int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
-                      const float* centroids, int32_t* labels, void* stream);
+                      const float* centroids, int precision, int32_t* labels, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /*
  * Stable counting sort of labels: sizes [bh,k], offsets [bh,k+1], order [bh,n].

@@ -19,6 +19,7 @@ STATUS_NAMES = {
     -5: "SPR_ERR_TIMEOUT", -6: "SPR_ERR_UNIMPLEMENTED", -7: "SPR_ERR_WORKSPACE", -8: "SPR_ERR_ARG",
 }
 SPR_F32, SPR_BF16, SPR_F16 = 0, 1, 2
+PRECISION = {"tf32": 0, "fp32": 1}
 
 _P = C.c_void_p
 _I = C.c_int
@@ -31,8 +32,8 @@ PROTOTYPES = {
     "spr_version": (_I, []),
     "spr_last_error": (C.c_char_p, []),
     "spr_kmeans_workspace_bytes": (_SZ, [_I64, _I64, _I, _I]),
-    "spr_kmeans_lloyd": (_I, [_P, _I, _I64, _I64, _I, _I, _I, _F, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
-    "spr_kmeans_assign": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P]),
+    "spr_kmeans_lloyd": (_I, [_P, _I, _I64, _I64, _I, _I, _I, _F, _I, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "spr_kmeans_assign": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _I, _P, _P, _SZ, _P]),
     "spr_label_sort": (_I, [_P, _I64, _I64, _I, _P, _P, _P, _P, _SZ, _P]),
     "spr_centroid_means": (_I, [_P, _I, _P, _P, _I64, _I64, _I, _I, _P, _P, _P, _P]),
     "spr_permute_rows": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _I, _P]),

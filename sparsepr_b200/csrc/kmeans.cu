@@ -224,12 +224,30 @@ using namespace spr;
 
 static int sort_chunks(int64_t n) { return (int)((n + kSortChunk - 1) / kSortChunk); }
 
+// Workspace layout shared by the k-means entry points.
+struct KmeansWs {
+  int* err;          // device status word of the last call (0 = ok)
+  int* done;         // convergence flag
+  float* shifts;     // per-iteration max centroid shift
+  float* csq;        // |c|^2 per centroid
+  int32_t* counts;   // per-(cluster, chunk) counts / starts of the label sort
+  float* next;       // updated centroids
+};
+
+static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
+  KmeansWs w;
+  w.err = c.take<int>(16);
+  w.done = c.take<int>(4);
+  w.shifts = c.take<float>(1024);
+  w.csq = c.take<float>((size_t)bh * k);
+  w.counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
+  w.next = c.take<float>((size_t)bh * k * d);
+  return w;
+}
+
 extern "C" size_t spr_kmeans_workspace_bytes(int64_t bh, int64_t n, int d, int k) {
   Carver c(nullptr, 0);
-  c.take<int32_t>((size_t)bh * k * sort_chunks(n));  // chunk counts / starts
-  c.take<float>((size_t)bh * k * d);                  // next centroids
-  c.take<float>(1024);                                // per-iteration shifts
-  c.take<int>(4);                                     // done flag
+  carve_kmeans(c, bh, n, d, k);
   return c.off + 256;
 }
 
@@ -264,7 +282,7 @@ static int validate_kmeans(int x_dtype, int64_t bh, int64_t n, int d, int k) {
   if (k > 8192) return fail(SPR_ERR_SHAPE, "k-means: k=%d exceeds 8192", k);
   if (x_dtype != SPR_F32 && x_dtype != SPR_BF16 && x_dtype != SPR_F16)
     return fail(SPR_ERR_DTYPE, "k-means: unsupported dtype %d", x_dtype);
-  if (!assign_supported_dim(d)) return fail(SPR_ERR_SHAPE, "k-means: d=%d unsupported (16,32,48,64,96,128)", d);
+  if (!assign_supported_dim(d)) return fail(SPR_ERR_SHAPE, "k-means: d=%d unsupported (multiple of 4, at most 128)", d);
   return SPR_OK;
 }
 
@@ -292,10 +310,18 @@ static int seg_mean_dispatch(int x_dtype, const void* x, const int32_t* order, c
 }
 
 extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
-                                 const float* centroids, int32_t* labels, void* stream) {
+                                 const float* centroids, int precision, int32_t* labels, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
-  return launch_assign(x, x_dtype, bh, n, d, k, centroids, labels, nullptr, (cudaStream_t)stream);
+  if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
+    return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);
+  Carver c(workspace, workspace_bytes);
+  KmeansWs w = carve_kmeans(c, bh, n, d, k);
+  if (!c.ok() || !workspace) return fail(SPR_ERR_WORKSPACE, "k-means assign: workspace %zu < %zu", workspace_bytes, c.off);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaMemsetAsync(w.err, 0, sizeof(int), st);
+  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.csq, precision, labels, nullptr, w.err, st);
 }
 
 extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
@@ -303,32 +329,35 @@ extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int 
                               void* stream) {
   if (bh <= 0 || n <= 0 || k <= 0 || k > 8192 || bh > 65535) return fail(SPR_ERR_SHAPE, "label sort: bad shape");
   Carver c(workspace, workspace_bytes);
-  int32_t* counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
+  KmeansWs w = carve_kmeans(c, bh, n, 0, k);
   if (!c.ok() || !workspace)
     return fail(SPR_ERR_WORKSPACE, "label sort: workspace %zu < %zu", workspace_bytes, c.off);
-  return launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, nullptr, (cudaStream_t)stream);
+  return launch_label_sort(labels, bh, n, k, sizes, offsets, order, w.counts, nullptr, (cudaStream_t)stream);
 }
 
 extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, int iters,
-                                float tol, int centroid_round_dtype, float* centroids, int32_t* labels,
+                                float tol, int centroid_round_dtype, int precision, float* centroids, int32_t* labels,
                                 int32_t* sizes, int32_t* offsets, int32_t* order, int32_t* iters_done,
                                 void* workspace, size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
   if (iters < 1 || iters > 1024) return fail(SPR_ERR_ARG, "k-means: iters=%d must be in [1,1024]", iters);
+  if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
+    return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);
   cudaStream_t st = (cudaStream_t)stream;
   Carver c(workspace, workspace_bytes);
-  int32_t* counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
-  float* next = c.take<float>((size_t)bh * k * d);
-  float* shifts = c.take<float>(1024);
-  int* done = c.take<int>(4);
+  KmeansWs w = carve_kmeans(c, bh, n, d, k);
   if (!c.ok() || !workspace) return fail(SPR_ERR_WORKSPACE, "k-means: workspace %zu < %zu", workspace_bytes, c.off);
-  cudaMemsetAsync(shifts, 0, 1024 * sizeof(float), st);
-  cudaMemsetAsync(done, 0, 4 * sizeof(int), st);
+  int32_t* counts = w.counts;
+  float* next = w.next;
+  float* shifts = w.shifts;
+  int* done = w.done;
+  // err, done and shifts are adjacent: one memset clears them.
+  cudaMemsetAsync(w.err, 0, (size_t)((char*)(w.shifts + 1024) - (char*)w.err), st);
   cudaMemsetAsync(iters_done, 0, sizeof(int32_t), st);
   const int64_t count = bh * k * (int64_t)d;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, labels, done, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.csq, precision, labels, done, w.err, st))) return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))

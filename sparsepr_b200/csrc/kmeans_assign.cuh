@@ -1,105 +1,278 @@
-// k-means assignment: per point, argmin over centroids of
+// k-means assignment on the tensor cores: per point, argmin over centroids of
 // max(|x|^2 + |c|^2 - 2 x.c, 0), ties to the lowest centroid index.
+//
+// The cross term x.c is a tcgen05 GEMM (kind::tf32, fp32 accumulation in
+// TMEM): 128 points x 128 centroids per MMA tile, the feature dimension padded
+// with zeros to a multiple of 32.  Precision SPR_KMEANS_TF32 matches the
+// reference's TF32 `tl.dot`; SPR_KMEANS_FP32 splits both operands as
+// hi = tf32(v), lo = v - hi and accumulates hi.hi + hi.lo + lo.hi (3xTF32),
+// which reproduces fp32 dot products to ~2^-22 relative.
+//
+// Warp roles (256 threads): warps 0-3 argmin epilogue (thread = point = TMEM
+// lane), warp 4 MMA issuer, warps 5-7 centroid-tile loaders (fp32 registers ->
+// swizzled shared memory, 2-stage ring).  TMEM holds two 128-column
+// accumulators so the epilogue of one centroid tile overlaps the next GEMM.
 #pragma once
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace spr {
 
-inline bool assign_supported_dim(int d) {
-  return d == 16 || d == 32 || d == 48 || d == 64 || d == 96 || d == 128;
+inline bool assign_supported_dim(int d) { return d >= 4 && d <= 128 && d % 4 == 0; }
+
+constexpr int kAsgM = 128;   // points per CTA
+constexpr int kAsgN = 128;   // centroids per tile
+constexpr int kAsgThreads = 256;
+constexpr int kAsgLoaders = 96;
+constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
+
+template <int DP, bool SPLIT>
+struct AsgSmem {
+  static constexpr int kRowBytes = DP * 4;
+  static constexpr int kXBytes = kAsgM * kRowBytes;
+  static constexpr int kCBytes = kAsgN * kRowBytes;
+  static constexpr int kParts = SPLIT ? 2 : 1;
+  static constexpr int kTotal = 1024 + kParts * kXBytes + 2 * kParts * kCBytes;
+};
+
+__device__ __forceinline__ float tf32_hi(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
 }
 
-constexpr int kAssignPoints = 128;   // points (threads) per block
-constexpr int kAssignTileK = 64;     // centroids per shared-memory tile
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+template <>
+__device__ __forceinline__ float4 load4<__half>(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __half2 a = *reinterpret_cast<const __half2*>(&u.x);
+  const __half2 b = *reinterpret_cast<const __half2*>(&u.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
 
-// Exact fp32 FFMA assignment.  Each thread keeps its point in registers and
-// streams centroid tiles from shared memory (broadcast reads).
-template <int D, typename T>
-__global__ void __launch_bounds__(kAssignPoints)
-assign_simt_kernel(const T* __restrict__ x, int64_t n, int k, const float* __restrict__ centroids,
-                   int32_t* __restrict__ labels, const int* __restrict__ done) {
-  if (done && *done) return;
-  __shared__ __align__(16) float sh_c[kAssignTileK * D];
-  __shared__ float sh_csq[kAssignTileK];
-  const int64_t b = blockIdx.y;
-  const int64_t p = (int64_t)blockIdx.x * kAssignPoints + threadIdx.x;
-  const bool valid = p < n;
-  float xr[D];
-  float xsq = 0.f;
-  const T* xp = x + (b * n + (valid ? p : 0)) * D;
-#pragma unroll
-  for (int e = 0; e < D; ++e) {
-    xr[e] = valid ? to_f32(xp[e]) : 0.f;
-    xsq = fmaf(xr[e], xr[e], xsq);
+// Store a float4 (optionally split into tf32 hi/lo parts) at a swizzled chunk.
+template <bool SPLIT>
+__device__ __forceinline__ void put4(uint32_t hi_base, uint32_t lo_base, uint32_t off, float4 v) {
+  if constexpr (SPLIT) {
+    const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+    const float4 l = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(hi_base + off), "f"(h.x), "f"(h.y), "f"(h.z), "f"(h.w)
+                 : "memory");
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(lo_base + off), "f"(l.x), "f"(l.y), "f"(l.z), "f"(l.w)
+                 : "memory");
+  } else {
+    (void)lo_base;
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(hi_base + off), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
   }
-  float best = 3.4e38f;
-  int best_idx = 0;
-  const float* cb = centroids + b * (int64_t)k * D;
-  for (int k0 = 0; k0 < k; k0 += kAssignTileK) {
-    const int tk = min(kAssignTileK, k - k0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < tk * D / 4; i += kAssignPoints)
-      reinterpret_cast<float4*>(sh_c)[i] = reinterpret_cast<const float4*>(cb + (int64_t)k0 * D)[i];
-    __syncthreads();
-    if (threadIdx.x < tk) {
-      float s = 0.f;
-      const float* cc = sh_c + threadIdx.x * D;
-      for (int e = 0; e < D; ++e) s = fmaf(cc[e], cc[e], s);
-      sh_csq[threadIdx.x] = s;
-    }
-    __syncthreads();
-    for (int j = 0; j < tk; ++j) {
-      const float4* c4 = reinterpret_cast<const float4*>(sh_c + j * D);
-      float dot0 = 0.f, dot1 = 0.f;
+}
+
+// |c|^2 per centroid, fp32 (one warp per centroid).
+__global__ void centroid_sq_kernel(const float* __restrict__ c, int64_t count, int d, float* __restrict__ csq,
+                                   const int* __restrict__ done) {
+  if (done && *done) return;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= count) return;
+  float s = 0.f;
+  for (int e = lane; e < d; e += 32) s = fmaf(c[w * d + e], c[w * d + e], s);
 #pragma unroll
-      for (int e = 0; e < D / 4; e += 2) {
-        const float4 a = c4[e];
-        dot0 = fmaf(xr[4 * e + 0], a.x, dot0);
-        dot0 = fmaf(xr[4 * e + 1], a.y, dot0);
-        dot0 = fmaf(xr[4 * e + 2], a.z, dot0);
-        dot0 = fmaf(xr[4 * e + 3], a.w, dot0);
-        if (e + 1 < D / 4) {
-          const float4 bq = c4[e + 1];
-          dot1 = fmaf(xr[4 * e + 4], bq.x, dot1);
-          dot1 = fmaf(xr[4 * e + 5], bq.y, dot1);
-          dot1 = fmaf(xr[4 * e + 6], bq.z, dot1);
-          dot1 = fmaf(xr[4 * e + 7], bq.w, dot1);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) csq[w] = s;
+}
+
+template <int DP, bool SPLIT, typename T>
+__global__ void __launch_bounds__(kAsgThreads, 1)
+assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* __restrict__ centroids,
+                 const float* __restrict__ csq, int32_t* __restrict__ labels, const int* __restrict__ done,
+                 int* __restrict__ err) {
+  using L = AsgSmem<DP, SPLIT>;
+  if (done && *done) return;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_c_full[2], bar_c_empty[2], bar_d_full[2], bar_d_free[2];
+  __shared__ uint32_t s_tmem;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sx_hi = tc::smem_addr(smem);
+  const uint32_t sx_lo = sx_hi + (SPLIT ? L::kXBytes : 0);
+  const uint32_t sc0 = sx_hi + L::kParts * L::kXBytes;  // stage s: hi at sc0 + s*parts*C, lo after hi
+  const int64_t b = blockIdx.y;
+  const int64_t p0 = (int64_t)blockIdx.x * kAsgM;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ntiles = (k + kAsgN - 1) / kAsgN;
+  constexpr int kChunks = DP / 4;  // 16-byte chunks per row
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_c_full[i], kAsgLoaders);
+      tc::mbar_init(&bar_c_empty[i], 1);
+      tc::mbar_init(&bar_d_full[i], 1);
+      tc::mbar_init(&bar_d_free[i], 128);
+    }
+    tc::mbar_fence_init();
+  }
+  if (warp == 4) tc::tmem_alloc<256>(&s_tmem);
+  // Point tile (all threads), zero padding past d and past n.
+  const T* xb = x + b * n * d;
+  for (int i = tid; i < kAsgM * kChunks; i += kAsgThreads) {
+    const int r = i / kChunks, ch = i % kChunks;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p0 + r < n && ch * 4 < d) v = load4<T>(xb + (p0 + r) * d + ch * 4);
+    put4<SPLIT>(sx_hi, sx_lo, tc::sw128_off(r, ch, kAsgM), v);
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp >= 5) {
+    // ---------------------------------------------------------- centroid loaders
+    const int lt = tid - 5 * 32;
+    const float* cb = centroids + b * (int64_t)k * d;
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t & 1;
+      if (t >= 2) tc::mbar_wait(&bar_c_empty[st], ((t >> 1) - 1) & 1, err, 11);
+      const uint32_t hi = sc0 + st * L::kParts * L::kCBytes;
+      const uint32_t lo = hi + (SPLIT ? L::kCBytes : 0);
+      const int k0 = t * kAsgN;
+      for (int i = lt; i < kAsgN * kChunks; i += kAsgLoaders) {
+        const int r = i / kChunks, ch = i % kChunks;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k0 + r < k && ch * 4 < d) v = *reinterpret_cast<const float4*>(cb + (int64_t)(k0 + r) * d + ch * 4);
+        put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgN), v);
+      }
+      tc::fence_proxy_async_smem();
+      tc::mbar_arrive(&bar_c_full[st]);
+    }
+  } else if (warp == 4) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t & 1;
+        if (!tc::mbar_wait(&bar_c_full[st], (t >> 1) & 1, err, 12)) break;
+        if (t >= 2 && !tc::mbar_wait(&bar_d_free[st], ((t >> 1) - 1) & 1, err, 12)) break;
+        tc::tc_fence_after();
+        const uint32_t chi = sc0 + st * L::kParts * L::kCBytes;
+        const uint32_t clo = chi + (SPLIT ? L::kCBytes : 0);
+        const uint32_t dt = tmem + st * 128;
+#pragma unroll
+        for (int kk = 0; kk < DP / 8; ++kk) {  // 8 tf32 = 32 bytes per MMA K step
+          const uint32_t kb = kk * 32;
+          const uint32_t oa = (kb >> 7) * (kAsgM * 128) + (kb & 127);
+          const uint32_t ob = (kb >> 7) * (kAsgN * 128) + (kb & 127);
+          tc::mma_tf32(dt, tc::sw128_desc(sx_hi + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg,
+                       kk > 0);
+          if constexpr (SPLIT) {
+            tc::mma_tf32(dt, tc::sw128_desc(sx_hi + oa, 16, 1024), tc::sw128_desc(clo + ob, 16, 1024), kIdescAsg, 1);
+            tc::mma_tf32(dt, tc::sw128_desc(sx_lo + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg, 1);
+          }
+        }
+        tc::mma_commit(&bar_d_full[st]);
+        tc::mma_commit(&bar_c_empty[st]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- argmin epilogue
+    const int row = tid;
+    const int64_t p = p0 + row;
+    float xsq = 0.f;
+    if (p < n) {
+      const T* xr = xb + p * d;
+      for (int e = 0; e < d; ++e) {
+        const float v = to_f32(xr[e]);
+        xsq = fmaf(v, v, xsq);
+      }
+    }
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const float* cs = csq + b * (int64_t)k;
+    float best = 3.4e38f;
+    int best_idx = 0;
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t & 1;
+      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[st], (t >> 1) & 1, err, 13));
+      if (!ok) break;
+      tc::tc_fence_after();
+      const int k0 = t * kAsgN;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float acc[32];
+        tc::tmem_ld32(tmem + lane_base + st * 128 + cb * 32, acc);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int kc = k0 + cb * 32 + j;
+          if (kc < k) {
+            const float dist = fmaxf(xsq + __ldg(cs + kc) - 2.f * acc[j], 0.f);
+            if (dist < best) {
+              best = dist;
+              best_idx = kc;
+            }
+          }
         }
       }
-      const float dist = fmaxf(xsq + sh_csq[j] - 2.f * (dot0 + dot1), 0.f);
-      if (dist < best) {
-        best = dist;
-        best_idx = k0 + j;
-      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bar_d_free[st]);
     }
+    if (p < n) labels[b * n + p] = best_idx;
   }
-  if (valid) labels[b * n + p] = best_idx;
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc<256>(tmem);
+  }
 }
 
-template <int D>
-static int launch_assign_d(const void* x, int x_dtype, int64_t bh, int64_t n, int k, const float* c,
-                           int32_t* labels, const int* done, cudaStream_t st) {
-  dim3 grid((unsigned)((n + kAssignPoints - 1) / kAssignPoints), (unsigned)bh);
-  if (x_dtype == SPR_F32)
-    assign_simt_kernel<D, float><<<grid, kAssignPoints, 0, st>>>((const float*)x, n, k, c, labels, done);
-  else if (x_dtype == SPR_BF16)
-    assign_simt_kernel<D, __nv_bfloat16><<<grid, kAssignPoints, 0, st>>>((const __nv_bfloat16*)x, n, k, c, labels, done);
-  else
-    assign_simt_kernel<D, __half><<<grid, kAssignPoints, 0, st>>>((const __half*)x, n, k, c, labels, done);
-  return check_launch("k-means assign");
+template <int DP, bool SPLIT, typename T>
+static int launch_assign_tc(const void* x, int64_t bh, int64_t n, int d, int k, const float* c, const float* csq,
+                            int32_t* labels, const int* done, int* err, cudaStream_t st) {
+  constexpr int smem = AsgSmem<DP, SPLIT>::kTotal;
+  auto kern = assign_tc_kernel<DP, SPLIT, T>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((unsigned)((n + kAsgM - 1) / kAsgM), (unsigned)bh);
+  kern<<<grid, kAsgThreads, smem, st>>>((const T*)x, n, d, k, c, csq, labels, done, err);
+  return check_launch("k-means assign (tcgen05)");
 }
 
+template <bool SPLIT, typename T>
+static int launch_assign_dp(const void* x, int64_t bh, int64_t n, int d, int k, const float* c, const float* csq,
+                            int32_t* labels, const int* done, int* err, cudaStream_t st) {
+  if (d <= 32) return launch_assign_tc<32, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  if (d <= 64) return launch_assign_tc<64, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  if constexpr (!SPLIT) {
+    if (d <= 96) return launch_assign_tc<96, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+    return launch_assign_tc<128, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  } else {
+    return fail(SPR_ERR_UNIMPLEMENTED, "k-means assign: fp32 (3xTF32) precision supports d <= 64, got d=%d", d);
+  }
+}
+
+// |c|^2 into csq (caller scratch of bh*k floats), then the assignment GEMM.
 inline int launch_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, const float* c,
-                         int32_t* labels, const int* done, cudaStream_t st) {
-  switch (d) {
-    case 16: return launch_assign_d<16>(x, x_dtype, bh, n, k, c, labels, done, st);
-    case 32: return launch_assign_d<32>(x, x_dtype, bh, n, k, c, labels, done, st);
-    case 48: return launch_assign_d<48>(x, x_dtype, bh, n, k, c, labels, done, st);
-    case 64: return launch_assign_d<64>(x, x_dtype, bh, n, k, c, labels, done, st);
-    case 96: return launch_assign_d<96>(x, x_dtype, bh, n, k, c, labels, done, st);
-    case 128: return launch_assign_d<128>(x, x_dtype, bh, n, k, c, labels, done, st);
-    default: return fail(SPR_ERR_SHAPE, "k-means assign: unsupported d=%d", d);
-  }
+                         float* csq, int precision, int32_t* labels, const int* done, int* err, cudaStream_t st) {
+  const int64_t count = bh * k;
+  centroid_sq_kernel<<<(unsigned)((count * 32 + 255) / 256), 256, 0, st>>>(c, count, d, csq, done);
+  int s = check_launch("centroid norms");
+  if (s) return s;
+  const bool split = precision == SPR_KMEANS_FP32;
+  if (x_dtype == SPR_F32)
+    return split ? launch_assign_dp<true, float>(x, bh, n, d, k, c, csq, labels, done, err, st)
+                 : launch_assign_dp<false, float>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  if (x_dtype == SPR_BF16)
+    return split ? launch_assign_dp<true, __nv_bfloat16>(x, bh, n, d, k, c, csq, labels, done, err, st)
+                 : launch_assign_dp<false, __nv_bfloat16>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  return split ? launch_assign_dp<true, __half>(x, bh, n, d, k, c, csq, labels, done, err, st)
+               : launch_assign_dp<false, __half>(x, bh, n, d, k, c, csq, labels, done, err, st);
 }
 
 }  // namespace spr

@@ -163,6 +163,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ uint32_t sw128_off(int row, int chunk, int rows) {
   return (uint32_t)((chunk >> 3) * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
+// The same layout for any row width that is a multiple of 128 bytes: 16-byte
+// chunk `chunk` of the row lives in 128-byte column block chunk/8, each block
+// holding all `rows` rows.  K-major UMMA descriptor for the K step that starts
+// at byte `kbyte` of the row: start = base + (kbyte/128)*rows*128 + kbyte%128,
+// LBO 16 (unused), SBO 1024.
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;

@@ -54,22 +54,42 @@ def workspace(dev: torch.device, nbytes: int, tag: str = "default") -> torch.Ten
     return buf
 
 
-def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor) -> torch.Tensor:
-    """Nearest centroid per point (ties -> lowest index): x [B,N,D], c [B,K,D] fp32 -> int32 [B,N]."""
+def _precision(p: str) -> int:
+    if p not in _lib.PRECISION:
+        raise ValueError(f"k-means precision must be one of {sorted(_lib.PRECISION)}, got {p!r}")
+    return _lib.PRECISION[p]
+
+
+def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor, precision: str = "tf32") -> torch.Tensor:
+    """Nearest centroid per point (ties -> lowest index): x [B,N,D], c [B,K,D] fp32 -> int32 [B,N].
+
+    ``precision``: "tf32" (tensor-core TF32 dot products, the reference GPU
+    behaviour) or "fp32" (3xTF32, fp32-accurate, d <= 64)."""
     dev = _cuda(x, centroids)
     b, n, d = x.shape
     k = centroids.shape[1]
     if centroids.shape != (b, k, d) or centroids.dtype != torch.float32:
         raise RuntimeError(f"centroids must be fp32 [B,K,D]={b, k, d}, got {tuple(centroids.shape)} {centroids.dtype}")
     labels = torch.empty((b, n), dtype=torch.int32, device=dev)
-    _count(1)
+    nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
+    ws = workspace(dev, nbytes, "kmeans")
+    _count(2)
     _lib.call("spr_kmeans_assign", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, _p(_contig("centroids", centroids)),
-              _p(labels), _stream(dev))
+              _precision(precision), _p(labels), _p(ws), ws.numel(), _stream(dev))
     return labels
 
 
+def kmeans_error_code(dev: torch.device) -> int:
+    """Device status word of the last k-means call on ``dev`` (0 = ok).  Synchronises; for tests."""
+    ws = _WS.get((dev.type, dev.index, "kmeans"))
+    if ws is None:
+        return 0
+    torch.cuda.synchronize(dev)
+    return int(ws[:4].view(torch.int32).item())
+
+
 def kmeans_lloyd(x: torch.Tensor, init_centroids: torch.Tensor, iters: int, tol: float = 0.0,
-                 round_centroids_to_input: bool = False):
+                 round_centroids_to_input: bool = False, precision: str = "tf32"):
     """Batched Lloyd k-means with an on-device ``tol`` stop.
 
     Returns ``(labels i32 [B,N], centroids f32 [B,K,D], sizes i32 [B,K],
@@ -89,8 +109,9 @@ def kmeans_lloyd(x: torch.Tensor, init_centroids: torch.Tensor, iters: int, tol:
     nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
     ws = workspace(dev, nbytes, "kmeans")
     rd = _DT[x.dtype] if round_centroids_to_input else _lib.SPR_F32
-    _count(6 * int(iters))
+    _count(7 * int(iters))
     _lib.call("spr_kmeans_lloyd", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, int(iters), float(tol), rd,
+              _precision(precision),
               _p(cent), _p(labels), _p(sizes), _p(offsets), _p(order), _p(iters_done), _p(ws), ws.numel(),
               _stream(dev))
     return labels, cent, sizes, offsets, order, iters_done

@@ -17,7 +17,8 @@ __all__ = ["batch_kmeans_Euclid", "FlashKMeans"]
 
 
 def batch_kmeans_Euclid(x, n_clusters, max_iters=100, tol=1e-4, init_centroids=None, verbose=False,
-                        backend="b200", *, seed: int = 0, round_centroids_to_input: bool = False):
+                        backend="b200", *, seed: int = 0, round_centroids_to_input: bool = False,
+                        precision: str = "tf32"):
     """Batched Lloyd k-means.
 
     Returns ``(cluster_ids int32 [B,N], centroids fp32 [B,K,D], cluster_sizes
@@ -40,11 +41,11 @@ def batch_kmeans_Euclid(x, n_clusters, max_iters=100, tol=1e-4, init_centroids=N
         init_centroids = torch.gather(x, 1, idx.unsqueeze(-1).expand(-1, -1, d))
     init = init_centroids.reshape(b, n_clusters, d).float()
     if max_iters == 0:
-        labels = K.kmeans_assign(x.contiguous(), init.contiguous())
+        labels = K.kmeans_assign(x.contiguous(), init.contiguous(), precision)
         sizes, _off, _ord = K.label_sort(labels, n_clusters)
         return labels, init, sizes, torch.zeros(1, dtype=torch.int32, device=x.device)
     labels, cent, sizes, _off, _order, iters = K.kmeans_lloyd(
-        x.contiguous(), init, max_iters, tol, round_centroids_to_input=round_centroids_to_input)
+        x.contiguous(), init, max_iters, tol, round_centroids_to_input=round_centroids_to_input, precision=precision)
     return labels, cent, sizes, iters
 
 

@@ -30,7 +30,10 @@ class N8V6Config:
     ``kmeans_backend``, ``compile_role_kv_projection``) are accepted for
     drop-in compatibility and have no effect here.  Added fields:
     ``kmeans_tol`` (the reference's implicit ``batch_kmeans_Euclid`` default
-    1e-4) and ``kmeans_init_seed`` (seed of the cold-start random-sample init).
+    1e-4), ``kmeans_init_seed`` (seed of the cold-start random-sample init)
+    and ``kmeans_precision`` ("tf32" like the reference's Triton ``tl.dot``,
+    or "fp32" for 3xTF32 distances that match an fp32 reference bit for bit
+    away from near ties).
     """
 
     num_q_centroids: int = 300
@@ -78,6 +81,7 @@ class N8V6Config:
     profile_breakdown: bool = False
     kmeans_tol: float = 1e-4
     kmeans_init_seed: int = 0
+    kmeans_precision: str = "tf32"
 
     def validate(self, head_dim: int | None = None) -> None:
         """Same checks and messages as ``n8_v6.py:281-348``."""
@@ -119,6 +123,8 @@ class N8V6Config:
                 "Adaptive budget densities must satisfy 0 <= minimum <= maximum <= 1; got "
                 f"minimum={self.adaptive_budget_min_density}, maximum={self.adaptive_budget_max_density}."
             )
+        if self.kmeans_precision not in {"tf32", "fp32"}:
+            raise ValueError(f"kmeans_precision must be tf32 or fp32; got {self.kmeans_precision!r}.")
         if self.probe_selection_policy not in {"role_equal_centroid", "first_token_largest_groups"}:
             raise ValueError(
                 "probe_selection_policy must be role_equal_centroid or first_token_largest_groups; got "
@@ -452,7 +458,8 @@ class N8V6Core:
         if k_init_features is None:
             idx = _init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev)
             k_init_features = torch.gather(k_feat, 1, idx.unsqueeze(-1).expand(-1, -1, k_feat.shape[-1]))
-        k_labels, _kc, k_sizes, k_off, k_order, k_it = K.kmeans_lloyd(k_feat, k_init_features, iters, cfg.kmeans_tol)
+        k_labels, _kc, k_sizes, k_off, k_order, k_it = K.kmeans_lloyd(k_feat, k_init_features, iters, cfg.kmeans_tol,
+                                                                     precision=cfg.kmeans_precision)
 
         # Original-space K/V centroids fused with the K/V permute (n8_v6.py:734-741, 905-934).
         use_full = k_full_source is not None or v_full_source is not None
@@ -486,7 +493,8 @@ class N8V6Core:
         if q_init_features is None:
             idx = _init_indices(bh, tokens, cfg.num_q_centroids, cfg.kmeans_init_seed + 1, dev)
             q_init_features = torch.gather(q_feat, 1, idx.unsqueeze(-1).expand(-1, -1, q_feat.shape[-1]))
-        q_labels, _qc, q_sizes, q_off, q_order, q_it = K.kmeans_lloyd(q_feat, q_init_features, iters, cfg.kmeans_tol)
+        q_labels, _qc, q_sizes, q_off, q_order, q_it = K.kmeans_lloyd(q_feat, q_init_features, iters, cfg.kmeans_tol,
+                                                                     precision=cfg.kmeans_precision)
         q_cent, q_perm = K.centroid_means(q, q_order, q_off, cfg.num_q_centroids, self.q_centroids, permute=True)
         self.q_centroids = q_cent
 

@@ -43,8 +43,8 @@ def test_version_and_error_message(lib):
                   None, 0, None)
     with pytest.raises(RuntimeError, match="SPR_ERR_WORKSPACE"):
         _lib.call("spr_label_sort", None, 1, 100, 4, None, None, None, None, 0, None)
-    with pytest.raises(RuntimeError, match="SPR_ERR_SHAPE.*d=40"):
-        _lib.call("spr_kmeans_assign", None, 0, 1, 10, 40, 4, None, None, None)
+    with pytest.raises(RuntimeError, match="SPR_ERR_SHAPE.*d=42"):
+        _lib.call("spr_kmeans_assign", None, 0, 1, 10, 42, 4, None, 0, None, None, 0, None)
 
 
 def test_workspace_queries(lib):

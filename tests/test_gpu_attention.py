@@ -100,7 +100,8 @@ def test_repair_apply_matches_oracle(cuda):
 
 def _cfg(**kw):
     base = dict(num_q_centroids=32, num_k_centroids=48, target_density=0.3, kmeans_iter_init=6, probe_rows=32,
-                repair_rank=16, selector_policy="attention_mass", role_kv_matmul_precision="highest", kmeans_tol=0.0)
+                repair_rank=16, selector_policy="attention_mass", role_kv_matmul_precision="highest", kmeans_tol=0.0,
+                kmeans_precision="fp32")
     base.update(kw)
     return N8V6Config(**base)
 

@@ -10,29 +10,37 @@ from sparsepr_b200.synthetic import synthetic_kmeans_points
 pytestmark = pytest.mark.gpu
 
 
-def _near_tie_free(x, c):
-    """Points whose best/second-best gap exceeds an fp32 rounding bound."""
+def _near_tie_free(x, c, rel):
+    """Points whose best/second-best gap exceeds a rounding bound of the distance."""
     gap = oracle.assign_margin(x, c)
     scale = (x.double() ** 2).sum(-1) + (c.double() ** 2).sum(-1).max(-1, keepdim=True).values
-    return gap > 1e-5 * scale
+    return gap > rel * scale
 
 
-@pytest.mark.parametrize("d,dtype", [(48, torch.float32), (64, torch.float32), (128, torch.bfloat16), (16, torch.float32)])
-def test_assign_matches_oracle(cuda, d, dtype):
+# fp32 (3xTF32) distances: exact labels off fp32 near ties.  tf32 (the
+# reference's GPU arithmetic): exact labels where the gap exceeds the TF32
+# dot-product error bound (~2^-9 of |x|^2 + |c|^2).
+@pytest.mark.parametrize("d,dtype,precision,rel", [
+    (48, torch.float32, "fp32", 1e-5), (64, torch.float32, "fp32", 1e-5), (16, torch.float32, "fp32", 1e-5),
+    (48, torch.float32, "tf32", 4e-3), (128, torch.bfloat16, "tf32", 4e-3), (96, torch.float32, "tf32", 4e-3),
+    (64, torch.bfloat16, "fp32", 1e-5)])
+def test_assign_matches_oracle(cuda, d, dtype, precision, rel):
     g = torch.Generator().manual_seed(d)
     x = torch.randn(3, 1537, d, generator=g).to(dtype)
-    c = torch.randn(3, 77, d, generator=g)
+    c = torch.randn(3, 300, d, generator=g)
     ref = oracle.euclid_assign(x, c)
-    got = K.kmeans_assign(x.to(cuda), c.to(cuda)).cpu().long()
-    ok = _near_tie_free(x, c)
-    assert ok.float().mean() > 0.95
+    got = K.kmeans_assign(x.to(cuda), c.to(cuda), precision).cpu().long()
+    assert K.kmeans_error_code(cuda) == 0
+    ok = _near_tie_free(x, c, rel)
+    assert ok.float().mean() > 0.5
     assert torch.equal(got[ok], ref[ok])
+    assert (got == ref).float().mean() > 0.98
 
 
 def test_assign_ties_go_to_lowest_index(cuda):
     x = torch.zeros(1, 64, 16)
     c = torch.zeros(1, 200, 16)  # every centroid equidistant
-    assert K.kmeans_assign(x.to(cuda), c.to(cuda)).max().item() == 0
+    assert K.kmeans_assign(x.to(cuda), c.to(cuda), "fp32").max().item() == 0
 
 
 @pytest.mark.parametrize("n,k", [(1, 1), (5000, 7), (70001, 1000), (4097, 3000)])
@@ -74,7 +82,7 @@ def test_kmeans_lloyd_matches_oracle(cuda):
     x = synthetic_kmeans_points(2, 64, (4, 12, 16), 24, dtype=torch.float32, seed=5)
     init = x[:, torch.randperm(x.shape[1], generator=torch.Generator().manual_seed(1))[:24]].clone()
     lr, cr, sr, itr = oracle.batch_kmeans_euclid(x, 24, 6, 0.0, init)
-    l, c, s, off, order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 6, 0.0)
+    l, c, s, off, order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 6, 0.0, precision="fp32")
     assert it.item() == itr == 6
     assert (l.cpu().long() == lr).float().mean() > 0.999
     if torch.equal(l.cpu().long(), lr):
@@ -87,7 +95,7 @@ def test_kmeans_tol_stops_on_device(cuda):
     x = synthetic_kmeans_points(1, 32, (2, 8, 8), 8, dtype=torch.float32, seed=2)
     init = x[:, :8].clone()
     _l, _c, _s, itr = oracle.batch_kmeans_euclid(x, 8, 40, 1e-3, init)
-    _l2, _c2, _s2, _off, _order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 40, 1e-3)
+    _l2, _c2, _s2, _off, _order, it = K.kmeans_lloyd(x.to(cuda), init.to(cuda), 40, 1e-3, precision="fp32")
     assert it.item() == itr < 40
 
 
