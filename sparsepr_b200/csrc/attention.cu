@@ -15,8 +15,11 @@
 //              permute is fused into the store).
 //   warp 4     MMA issuer (one thread): S(j) = Q K_j^T into one of two TMEM S
 //              buffers, O += P(j) V_j into the TMEM O accumulator.
-//   warps 5-7  loaders: gather the K/V rows of each key tile with 16-byte
-//              cp.async into a 2-stage ring (no index list is materialised).
+//   warps 5-8  loaders: gather the K/V rows of each key tile with 16-byte
+//              cp.async into a 2-stage ring.  The selected clusters' runs
+//              (start, prefix length) are staged in shared memory once per
+//              CTA; each loader lane resolves one key slot by binary search,
+//              and each warp instruction moves two full 256-byte rows.
 // TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O.
 // Operand tiles use the canonical 128-byte-swizzled K-major layout; V is the
 // MN-major B operand of the PV product.
@@ -30,8 +33,9 @@ constexpr int kD = 128;
 constexpr int kTileM = 128;
 constexpr int kTileN = 128;
 constexpr int kSoftmaxThreads = 128;
-constexpr int kLoaderThreads = 96;
-constexpr int kThreadsTc = 256;
+constexpr int kLoaderThreads = 128;
+constexpr int kThreadsTc = 288;
+constexpr int kMaxRuns = 2048;  // key clusters per problem (ck) this kernel accepts
 constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
 constexpr int kSmemTc = 1024 /*align slack*/ + kTileBytes /*Q*/ + 4 * kTileBytes /*K,V x2*/ + kTileBytes /*P*/;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
@@ -65,7 +69,8 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_kv_full[2], bar_kv_empty[2], bar_s_full[2], bar_p_full, bar_o_done;
   __shared__ uint32_t s_tmem;
-  __shared__ int32_t s_src[2][kTileN];
+  __shared__ int32_t s_run_start[kMaxRuns];
+  __shared__ int32_t s_run_end[kMaxRuns + 1];  // inclusive prefix of run lengths
   __shared__ int s_total;
 
   const int64_t b = blockIdx.y;
@@ -108,15 +113,29 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     mbar_fence_init();
   }
   if (warp == 4) tmem_alloc<512>(&s_tmem);
-  if (warp == 5) {  // total selected keys of this query cluster
-    int64_t t = 0;
-    for (int i = lane; i < nsel; i += 32) {
-      const int kc = ids[i];
-      t += ko[kc + 1] - ko[kc];
-    }
+  if (warp == 5) {  // run table of the selected key clusters: start row and prefix length
+    int carry = 0;
+    for (int base = 0; base < nsel; base += 32) {
+      const int i = base + lane;
+      int start = 0, len = 0;
+      if (i < nsel) {
+        const int kc = ids[i];
+        start = ko[kc];
+        len = ko[kc + 1] - start;
+      }
+      int incl = len;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (lane == 0) s_total = (int)t;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (i < nsel) {
+        s_run_start[i] = start;
+        s_run_end[i] = carry + incl;
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_total = carry;
   }
   // Q tile (all threads), zero rows past the cluster end.
   for (int i = tid; i < kTileM * 16; i += kThreadsTc) {
@@ -136,33 +155,31 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
   if (warp >= 5) {
     // ------------------------------------------------------------ loaders
-    const int lt = tid - 5 * 32;
-    int cur_pos = 0, cur_off = 0;  // run cursor, meaningful in lt == 0
+    const int lw = warp - 5;  // loader warp: rows [32*lw, 32*lw+32) of each key tile
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      if (lt == 0) {
-        bool ok = true;
-        if (j >= 2) ok = mbar_wait(&bar_kv_empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
-        int filled = 0;
-        while (ok && filled < kTileN && cur_pos < nsel) {
-          const int kc = ids[cur_pos];
-          const int32_t rb = ko[kc], re = ko[kc + 1];
-          const int32_t avail = (re - rb) - cur_off;
-          if (avail <= 0) { ++cur_pos; cur_off = 0; continue; }
-          const int take = min(avail, kTileN - filled);
-          for (int x = 0; x < take; ++x) s_src[st][filled + x] = rb + cur_off + x;
-          filled += take;
-          cur_off += take;
+      // Source row of key slot 32*lw + lane: binary search of the run table.
+      const int g = j * kTileN + lw * 32 + lane;
+      int src = -1;
+      if (g < total) {
+        int lo2 = 0, hi2 = nsel - 1;  // first run with end > g
+        while (lo2 < hi2) {
+          const int mid = (lo2 + hi2) >> 1;
+          if (s_run_end[mid] > g) hi2 = mid; else lo2 = mid + 1;
         }
-        for (int x = filled; x < kTileN; ++x) s_src[st][x] = -1;
+        const int prev = lo2 > 0 ? s_run_end[lo2 - 1] : 0;
+        src = s_run_start[lo2] + (g - prev);
       }
-      named_bar(1, kLoaderThreads);
+      if (j >= 2) mbar_wait(&bar_kv_empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
       const uint32_t dk = smem_addr(sK + st * kTileBytes), dv = smem_addr(sV + st * kTileBytes);
-      for (int i = lt; i < kTileN * 16; i += kLoaderThreads) {
-        const int r = i >> 4, ch = i & 15;
-        const int32_t src = s_src[st][r];
-        const bool ok = src >= 0;
-        const int64_t off = (int64_t)(ok ? src : 0) * kD + ch * 8;
+      const int half = lane >> 4, ch = lane & 15;
+#pragma unroll 4
+      for (int pr = 0; pr < 16; ++pr) {  // two rows per instruction: lanes 0-15 row 2pr, 16-31 row 2pr+1
+        const int rl = 2 * pr + half;
+        const int rsrc = __shfl_sync(0xffffffffu, src, rl);
+        const int r = lw * 32 + rl;
+        const bool ok = rsrc >= 0;
+        const int64_t off = (int64_t)(ok ? rsrc : 0) * kD + ch * 8;
         const uint32_t o = sw128_off(r, ch, kTileN);
         cp_async16(dk + o, kb + off, ok);
         cp_async16(dv + o, vb + off, ok);
@@ -330,6 +347,7 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
                                      int ck, const int32_t* q_order, void* out, void* workspace,
                                      size_t workspace_bytes, void* stream) {
   if (d != kD) return fail(SPR_ERR_SHAPE, "block-sparse attention requires d=128, got %d", d);
+  if (ck > kMaxRuns) return fail(SPR_ERR_SHAPE, "block-sparse attention: ck=%d exceeds %d", ck, kMaxRuns);
   if (bh <= 0 || nq <= 0 || nk <= 0 || cq <= 0 || ck <= 0 || bh > 65535 || nq > INT32_MAX || nk > INT32_MAX)
     return fail(SPR_ERR_SHAPE, "block-sparse attention: bad shape");
   if (!aligned(q_perm, 16) || !aligned(k_perm, 16) || !aligned(v_perm, 16) || !aligned(out, 16))

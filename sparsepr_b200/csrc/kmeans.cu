@@ -321,7 +321,7 @@ extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t
   if (!c.ok() || !workspace) return fail(SPR_ERR_WORKSPACE, "k-means assign: workspace %zu < %zu", workspace_bytes, c.off);
   cudaStream_t st = (cudaStream_t)stream;
   cudaMemsetAsync(w.err, 0, sizeof(int), st);
-  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.csq, precision, labels, nullptr, w.err, st);
+  return launch_assign(x, x_dtype, bh, n, d, k, centroids, precision, labels, nullptr, w.err, st);
 }
 
 extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
@@ -357,7 +357,7 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
   cudaMemsetAsync(iters_done, 0, sizeof(int32_t), st);
   const int64_t count = bh * k * (int64_t)d;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.csq, precision, labels, done, w.err, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, precision, labels, done, w.err, st))) return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))

@@ -8,9 +8,10 @@
 // hi = tf32(v), lo = v - hi and accumulates hi.hi + hi.lo + lo.hi (3xTF32),
 // which reproduces fp32 dot products to ~2^-22 relative.
 //
-// Warp roles (256 threads): warps 0-3 argmin epilogue (thread = point = TMEM
-// lane), warp 4 MMA issuer, warps 5-7 centroid-tile loaders (fp32 registers ->
-// swizzled shared memory, 2-stage ring).  TMEM holds two 128-column
+// Warp roles (288 threads): warps 0-3 argmin epilogue (thread = point = TMEM
+// lane), warp 4 MMA issuer, warps 5-8 centroid-tile loaders (thread =
+// centroid row: fp32 registers -> swizzled shared memory plus |c|^2, 2-stage
+// ring).  TMEM holds two 128-column
 // accumulators so the epilogue of one centroid tile overlaps the next GEMM.
 #pragma once
 #include "tc_common.cuh"
@@ -21,8 +22,8 @@ inline bool assign_supported_dim(int d) { return d >= 4 && d <= 128 && d % 4 == 
 
 constexpr int kAsgM = 128;   // points per CTA
 constexpr int kAsgN = 128;   // centroids per tile
-constexpr int kAsgThreads = 256;
-constexpr int kAsgLoaders = 96;
+constexpr int kAsgThreads = 288;
+constexpr int kAsgLoaders = 128;
 constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
 
 template <int DP, bool SPLIT>
@@ -78,30 +79,16 @@ __device__ __forceinline__ void put4(uint32_t hi_base, uint32_t lo_base, uint32_
   }
 }
 
-// |c|^2 per centroid, fp32 (one warp per centroid).
-__global__ void centroid_sq_kernel(const float* __restrict__ c, int64_t count, int d, float* __restrict__ csq,
-                                   const int* __restrict__ done) {
-  if (done && *done) return;
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= count) return;
-  float s = 0.f;
-  for (int e = lane; e < d; e += 32) s = fmaf(c[w * d + e], c[w * d + e], s);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) csq[w] = s;
-}
-
 template <int DP, bool SPLIT, typename T>
 __global__ void __launch_bounds__(kAsgThreads, 1)
 assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* __restrict__ centroids,
-                 const float* __restrict__ csq, int32_t* __restrict__ labels, const int* __restrict__ done,
-                 int* __restrict__ err) {
+                 int32_t* __restrict__ labels, const int* __restrict__ done, int* __restrict__ err) {
   using L = AsgSmem<DP, SPLIT>;
   if (done && *done) return;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_c_full[2], bar_c_empty[2], bar_d_full[2], bar_d_free[2];
   __shared__ uint32_t s_tmem;
+  __shared__ float s_csq[2][kAsgN];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sx_hi = tc::smem_addr(smem);
   const uint32_t sx_lo = sx_hi + (SPLIT ? L::kXBytes : 0);
@@ -138,20 +125,31 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
 
   if (warp >= 5) {
     // ---------------------------------------------------------- centroid loaders
-    const int lt = tid - 5 * 32;
+    const int r = tid - 5 * 32;  // centroid row of the tile owned by this thread
     const float* cb = centroids + b * (int64_t)k * d;
     for (int t = 0; t < ntiles; ++t) {
       const int st = t & 1;
-      if (t >= 2) tc::mbar_wait(&bar_c_empty[st], ((t >> 1) - 1) & 1, err, 11);
+      const int kc = t * kAsgN + r;
+      float4 v[kChunks];
+      float sq = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) {
+        v[ch] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kc < k && ch * 4 < d) v[ch] = *reinterpret_cast<const float4*>(cb + (int64_t)kc * d + ch * 4);
+        sq = fmaf(v[ch].x, v[ch].x, sq);
+        sq = fmaf(v[ch].y, v[ch].y, sq);
+        sq = fmaf(v[ch].z, v[ch].z, sq);
+        sq = fmaf(v[ch].w, v[ch].w, sq);
+      }
+      if (t >= 2) {  // the GEMM and the argmin of tile t-2 are both done with this stage
+        tc::mbar_wait(&bar_c_empty[st], ((t >> 1) - 1) & 1, err, 11);
+        tc::mbar_wait(&bar_d_free[st], ((t >> 1) - 1) & 1, err, 11);
+      }
       const uint32_t hi = sc0 + st * L::kParts * L::kCBytes;
       const uint32_t lo = hi + (SPLIT ? L::kCBytes : 0);
-      const int k0 = t * kAsgN;
-      for (int i = lt; i < kAsgN * kChunks; i += kAsgLoaders) {
-        const int r = i / kChunks, ch = i % kChunks;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k0 + r < k && ch * 4 < d) v = *reinterpret_cast<const float4*>(cb + (int64_t)(k0 + r) * d + ch * 4);
-        put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgN), v);
-      }
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgN), v[ch]);
+      s_csq[st][r] = sq;
       tc::fence_proxy_async_smem();
       tc::mbar_arrive(&bar_c_full[st]);
     }
@@ -186,16 +184,21 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
     // ---------------------------------------------------------- argmin epilogue
     const int row = tid;
     const int64_t p = p0 + row;
-    float xsq = 0.f;
-    if (p < n) {
-      const T* xr = xb + p * d;
-      for (int e = 0; e < d; ++e) {
-        const float v = to_f32(xr[e]);
-        xsq = fmaf(v, v, xsq);
-      }
+    float xsq = 0.f;  // |x|^2 of this point from the staged tile (hi + lo is exact)
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      float4 h, l = make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint32_t off = tc::sw128_off(row, ch, kAsgM);
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(h.x), "=f"(h.y), "=f"(h.z), "=f"(h.w) : "r"(sx_hi + off));
+      if constexpr (SPLIT)
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l.x), "=f"(l.y), "=f"(l.z), "=f"(l.w) : "r"(sx_lo + off));
+      const float4 v = make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
+      xsq = fmaf(v.x, v.x, xsq);
+      xsq = fmaf(v.y, v.y, xsq);
+      xsq = fmaf(v.z, v.z, xsq);
+      xsq = fmaf(v.w, v.w, xsq);
     }
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const float* cs = csq + b * (int64_t)k;
     float best = 3.4e38f;
     int best_idx = 0;
     for (int t = 0; t < ntiles; ++t) {
@@ -212,7 +215,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
         for (int j = 0; j < 32; ++j) {
           const int kc = k0 + cb * 32 + j;
           if (kc < k) {
-            const float dist = fmaxf(xsq + __ldg(cs + kc) - 2.f * acc[j], 0.f);
+            const float dist = fmaxf(xsq + s_csq[st][cb * 32 + j] - 2.f * acc[j], 0.f);
             if (dist < best) {
               best = dist;
               best_idx = kc;
@@ -234,45 +237,40 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
 }
 
 template <int DP, bool SPLIT, typename T>
-static int launch_assign_tc(const void* x, int64_t bh, int64_t n, int d, int k, const float* c, const float* csq,
+static int launch_assign_tc(const void* x, int64_t bh, int64_t n, int d, int k, const float* c,
                             int32_t* labels, const int* done, int* err, cudaStream_t st) {
   constexpr int smem = AsgSmem<DP, SPLIT>::kTotal;
   auto kern = assign_tc_kernel<DP, SPLIT, T>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((unsigned)((n + kAsgM - 1) / kAsgM), (unsigned)bh);
-  kern<<<grid, kAsgThreads, smem, st>>>((const T*)x, n, d, k, c, csq, labels, done, err);
+  kern<<<grid, kAsgThreads, smem, st>>>((const T*)x, n, d, k, c, labels, done, err);
   return check_launch("k-means assign (tcgen05)");
 }
 
 template <bool SPLIT, typename T>
-static int launch_assign_dp(const void* x, int64_t bh, int64_t n, int d, int k, const float* c, const float* csq,
+static int launch_assign_dp(const void* x, int64_t bh, int64_t n, int d, int k, const float* c,
                             int32_t* labels, const int* done, int* err, cudaStream_t st) {
-  if (d <= 32) return launch_assign_tc<32, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
-  if (d <= 64) return launch_assign_tc<64, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+  if (d <= 32) return launch_assign_tc<32, SPLIT, T>(x, bh, n, d, k, c, labels, done, err, st);
+  if (d <= 64) return launch_assign_tc<64, SPLIT, T>(x, bh, n, d, k, c, labels, done, err, st);
   if constexpr (!SPLIT) {
-    if (d <= 96) return launch_assign_tc<96, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
-    return launch_assign_tc<128, SPLIT, T>(x, bh, n, d, k, c, csq, labels, done, err, st);
+    if (d <= 96) return launch_assign_tc<96, SPLIT, T>(x, bh, n, d, k, c, labels, done, err, st);
+    return launch_assign_tc<128, SPLIT, T>(x, bh, n, d, k, c, labels, done, err, st);
   } else {
     return fail(SPR_ERR_UNIMPLEMENTED, "k-means assign: fp32 (3xTF32) precision supports d <= 64, got d=%d", d);
   }
 }
 
-// |c|^2 into csq (caller scratch of bh*k floats), then the assignment GEMM.
 inline int launch_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, const float* c,
-                         float* csq, int precision, int32_t* labels, const int* done, int* err, cudaStream_t st) {
-  const int64_t count = bh * k;
-  centroid_sq_kernel<<<(unsigned)((count * 32 + 255) / 256), 256, 0, st>>>(c, count, d, csq, done);
-  int s = check_launch("centroid norms");
-  if (s) return s;
+                         int precision, int32_t* labels, const int* done, int* err, cudaStream_t st) {
   const bool split = precision == SPR_KMEANS_FP32;
   if (x_dtype == SPR_F32)
-    return split ? launch_assign_dp<true, float>(x, bh, n, d, k, c, csq, labels, done, err, st)
-                 : launch_assign_dp<false, float>(x, bh, n, d, k, c, csq, labels, done, err, st);
+    return split ? launch_assign_dp<true, float>(x, bh, n, d, k, c, labels, done, err, st)
+                 : launch_assign_dp<false, float>(x, bh, n, d, k, c, labels, done, err, st);
   if (x_dtype == SPR_BF16)
-    return split ? launch_assign_dp<true, __nv_bfloat16>(x, bh, n, d, k, c, csq, labels, done, err, st)
-                 : launch_assign_dp<false, __nv_bfloat16>(x, bh, n, d, k, c, csq, labels, done, err, st);
-  return split ? launch_assign_dp<true, __half>(x, bh, n, d, k, c, csq, labels, done, err, st)
-               : launch_assign_dp<false, __half>(x, bh, n, d, k, c, csq, labels, done, err, st);
+    return split ? launch_assign_dp<true, __nv_bfloat16>(x, bh, n, d, k, c, labels, done, err, st)
+                 : launch_assign_dp<false, __nv_bfloat16>(x, bh, n, d, k, c, labels, done, err, st);
+  return split ? launch_assign_dp<true, __half>(x, bh, n, d, k, c, labels, done, err, st)
+               : launch_assign_dp<false, __half>(x, bh, n, d, k, c, labels, done, err, st);
 }
 
 }  // namespace spr

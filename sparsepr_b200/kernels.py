@@ -73,7 +73,7 @@ def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor, precision: str = "tf
     labels = torch.empty((b, n), dtype=torch.int32, device=dev)
     nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
     ws = workspace(dev, nbytes, "kmeans")
-    _count(2)
+    _count(1)
     _lib.call("spr_kmeans_assign", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, _p(_contig("centroids", centroids)),
               _precision(precision), _p(labels), _p(ws), ws.numel(), _stream(dev))
     return labels
@@ -109,7 +109,7 @@ def kmeans_lloyd(x: torch.Tensor, init_centroids: torch.Tensor, iters: int, tol:
     nbytes = _lib.query("spr_kmeans_workspace_bytes", b, n, d, k)
     ws = workspace(dev, nbytes, "kmeans")
     rd = _DT[x.dtype] if round_centroids_to_input else _lib.SPR_F32
-    _count(7 * int(iters))
+    _count(6 * int(iters))
     _lib.call("spr_kmeans_lloyd", _p(_contig("x", x)), _DT[x.dtype], b, n, d, k, int(iters), float(tol), rd,
               _precision(precision),
               _p(cent), _p(labels), _p(sizes), _p(offsets), _p(order), _p(iters_done), _p(ws), ws.numel(),
