@@ -163,6 +163,25 @@ int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_
 /* Scratch bytes needed by spr_block_sparse_attn. */
 size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq);
 
+/*
+ * spr_block_sparse_attn without a workspace, for callers that cannot allocate
+ * device memory (a host that owns all of HBM through its own pool, or a loop
+ * that must not call cudaMalloc and has no buffer to lend).  Same arguments and
+ * result as spr_block_sparse_attn minus the workspace.  Its scratch is a fixed
+ * library-owned device array of 65,536 tile-table entries: every GPU that loads
+ * the library keeps 256 KiB for it until the process exits, and calls with
+ * bh*(cq+1) > 65,536 are rejected with SPR_ERR_SHAPE.  The first call on a
+ * device looks up the array's device address (do it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race; the array keeps the last call's contents
+ * and each call rewrites what it reads.  No counterpart in the reference.
+ */
+int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_perm, const void* v_perm,
+                                  const int32_t* q_offsets, const int32_t* k_offsets,
+                                  const int32_t* sel_ids, const int32_t* sel_counts,
+                                  int64_t bh, int64_t nq, int64_t nk, int d, int cq, int ck,
+                                  const int32_t* q_order, void* out, void* stream);
+
 /* ---------------------------------------------------------------- small linear algebra */
 
 /*

@@ -371,3 +371,81 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
       sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
   return check_launch("block-sparse attention");
 }
+
+// ---------------------------------------------------------------------------
+// No-allocation variant.  Some callers cannot allocate device memory at all:
+// a host framework that hands every byte of HBM to its own pool and forbids
+// other allocations, or a latency-critical loop that may not call cudaMalloc
+// (it can synchronise the whole device) and has no buffer to lend as a
+// workspace.  For them the attention call below keeps its scratch (the status
+// word and the per-problem tile table) in a fixed array in device memory that
+// the library owns.
+//
+// The array is `static __device__`: every GPU that loads this library holds
+// its 256 KiB + 256 B until the process exits.  In host code its name is only
+// a host-side stand-in for the symbol, not a device address, so the host asks
+// the runtime for the real address once per device (cudaGetSymbolAddress with
+// that device current) and passes that pointer to the kernels.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace spr {
+constexpr int kNoAllocStatusInts = 64;       // status word + padding (keeps the table 256-byte aligned)
+constexpr int kNoAllocTableInts = 65536;     // maximum bh * (cq + 1)
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) int32_t g_attn_noalloc_scratch[kNoAllocStatusInts + kNoAllocTableInts];
+static std::mutex g_noalloc_mu;
+static int32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (set up on first use).
+static int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "no-alloc attention: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(SPR_ERR_ARG, "no-alloc attention: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(SPR_ERR_LAUNCH, "no-alloc attention: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return SPR_OK;
+}
+}  // namespace spr
+
+extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_perm, const void* v_perm,
+                                             const int32_t* q_offsets, const int32_t* k_offsets,
+                                             const int32_t* sel_ids, const int32_t* sel_counts, int64_t bh,
+                                             int64_t nq, int64_t nk, int d, int cq, int ck, const int32_t* q_order,
+                                             void* out, void* stream) {
+  if (d != kD) return fail(SPR_ERR_SHAPE, "block-sparse attention requires d=128, got %d", d);
+  if (ck > kMaxRuns) return fail(SPR_ERR_SHAPE, "block-sparse attention: ck=%d exceeds %d", ck, kMaxRuns);
+  if (bh <= 0 || nq <= 0 || nk <= 0 || cq <= 0 || ck <= 0 || bh > 65535 || nq > INT32_MAX || nk > INT32_MAX)
+    return fail(SPR_ERR_SHAPE, "block-sparse attention: bad shape");
+  if (bh * (int64_t)(cq + 1) > kNoAllocTableInts)
+    return fail(SPR_ERR_SHAPE,
+                "no-alloc attention: bh*(cq+1)=%lld exceeds the fixed scratch of %d entries; "
+                "use spr_block_sparse_attn with a caller workspace",
+                (long long)(bh * (int64_t)(cq + 1)), kNoAllocTableInts);
+  if (!aligned(q_perm, 16) || !aligned(k_perm, 16) || !aligned(v_perm, 16) || !aligned(out, 16))
+    return fail(SPR_ERR_ALIGN, "block-sparse attention: 16-byte alignment required");
+  int32_t* scratch = nullptr;
+  int s = noalloc_scratch(&scratch);
+  if (s) return s;
+  int* err = scratch;                               // zeroed by tile_table_kernel on every call
+  int32_t* tile_start = scratch + kNoAllocStatusInts;  // fully rewritten on every call
+  cudaStream_t st = (cudaStream_t)stream;
+  tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
+  if ((s = check_launch("attention tile table"))) return s;
+  cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+  const int64_t max_tiles = (nq + kTileM - 1) / kTileM + cq;
+  dim3 grid((unsigned)max_tiles, (unsigned)bh);
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
+  block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
+      (const __nv_bfloat16*)q_perm, (const __nv_bfloat16*)k_perm, (const __nv_bfloat16*)v_perm, q_offsets, k_offsets,
+      sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
+  return check_launch("block-sparse attention (no-alloc)");
+}
