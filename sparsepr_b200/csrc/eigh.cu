@@ -22,7 +22,7 @@ sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals,
   float* V = sh + kEigMax * kEigLd;     // [n][kEigLd]
   __shared__ float s_c[kEigMax / 2], s_s[kEigMax / 2];
   __shared__ int s_p[kEigMax / 2], s_q[kEigMax / 2];
-  __shared__ int s_arr[kEigMax];
+  __shared__ int s_rank[kEigMax];
   __shared__ float s_red[kEigThreads / 32][2];
   __shared__ int s_stop;
   const int64_t b = blockIdx.x;
@@ -33,7 +33,6 @@ sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals,
     A[i * kEigLd + j] = 0.5f * (src[i * n + j] + src[j * n + i]);
     V[i * kEigLd + j] = i == j ? 1.f : 0.f;
   }
-  for (int i = tid; i < n; i += blockDim.x) s_arr[i] = i;
   const int half = n / 2;
   __syncthreads();
   for (int sweep = 0; sweep < max_sweeps; ++sweep) {
@@ -61,7 +60,10 @@ sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals,
     if (s_stop) break;
     for (int round = 0; round < n - 1; ++round) {
       if (tid < half) {
-        int p = s_arr[tid], q = s_arr[n - 1 - tid];
+        // Round-robin schedule: slot 0 holds index 0, slot i >= 1 holds
+        // 1 + (i - 1 + round) mod (n - 1); pair t is (slot t, slot n-1-t).
+        auto slot = [&](int i) { return i == 0 ? 0 : 1 + (i - 1 + round) % (n - 1); };
+        int p = slot(tid), q = slot(n - 1 - tid);
         if (p > q) { const int t = p; p = q; q = t; }
         const float apq = A[p * kEigLd + q];
         float c = 1.f, s = 0.f;
@@ -97,12 +99,6 @@ sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals,
         V[i * kEigLd + q] = s * vp + c * vq;
       }
       __syncthreads();
-      if (tid == 0) {  // round-robin: keep slot 0, rotate the rest
-        const int last = s_arr[n - 1];
-        for (int i = n - 1; i > 1; --i) s_arr[i] = s_arr[i - 1];
-        s_arr[1] = last;
-      }
-      __syncthreads();
     }
   }
   // Ascending order of the diagonal (ties by index), eigenvectors follow.
@@ -114,13 +110,13 @@ sym_eig_kernel(const float* __restrict__ a_in, int n, float* __restrict__ evals,
       rank += (li < lj) || (li == lj && i < j);
     }
     evals[b * n + rank] = lj;
-    s_arr[j] = rank;
+    s_rank[j] = rank;
   }
   __syncthreads();
   float* out = evecs + b * (int64_t)n * n;
   for (int idx = tid; idx < n * n; idx += blockDim.x) {
     const int i = idx / n, j = idx % n;
-    out[i * n + s_arr[j]] = V[i * kEigLd + j];
+    out[i * n + s_rank[j]] = V[i * kEigLd + j];
   }
 }
 
