@@ -15,11 +15,14 @@
 //              permute is fused into the store).
 //   warp 4     MMA issuer (one thread): S(j) = Q K_j^T into one of two TMEM S
 //              buffers, O += P(j) V_j into the TMEM O accumulator.
-//   warps 5-8  loaders: gather the K/V rows of each key tile with 16-byte
-//              cp.async into a 2-stage ring.  The selected clusters' runs
-//              (start, prefix length) are staged in shared memory once per
-//              CTA; each loader lane resolves one key slot by binary search,
-//              and each warp instruction moves two full 256-byte rows.
+//   warps 5-8  loaders: warps 5-6 gather K rows, warps 7-8 V rows, each into
+//              its own 2-stage ring with 16-byte cp.async.  K stage j is freed
+//              as soon as S(j) is done and V stage j when PV(j) is done, so
+//              the gather latency of tile j+2 hides behind the MMAs of tiles
+//              j and j+1.  The selected clusters' runs (start, prefix length)
+//              are staged in shared memory once per CTA; each loader lane
+//              resolves one key slot by binary search, and each warp
+//              instruction moves two full 256-byte rows.
 // TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O.
 // Operand tiles use the canonical 128-byte-swizzled K-major layout; V is the
 // MN-major B operand of the PV product.
@@ -67,7 +70,8 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
                             int64_t nq, int64_t nk, int cq, int ck, const int32_t* __restrict__ q_order,
                             __nv_bfloat16* __restrict__ out, float scale_log2, int* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_kv_full[2], bar_kv_empty[2], bar_s_full[2], bar_p_full, bar_o_done;
+  __shared__ uint64_t bar_k_full[2], bar_k_empty[2], bar_v_full[2], bar_v_empty[2], bar_s_full[2], bar_p_full,
+      bar_o_done;
   __shared__ uint32_t s_tmem;
   __shared__ int32_t s_run_start[kMaxRuns];
   __shared__ int32_t s_run_end[kMaxRuns + 1];  // inclusive prefix of run lengths
@@ -104,8 +108,10 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar_kv_full[i], kLoaderThreads);
-      mbar_init(&bar_kv_empty[i], 1);
+      mbar_init(&bar_k_full[i], kLoaderThreads / 2);
+      mbar_init(&bar_v_full[i], kLoaderThreads / 2);
+      mbar_init(&bar_k_empty[i], 1);
+      mbar_init(&bar_v_empty[i], 1);
       mbar_init(&bar_s_full[i], 1);
     }
     mbar_init(&bar_p_full, kSoftmaxThreads);
@@ -155,39 +161,48 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
   if (warp >= 5) {
     // ------------------------------------------------------------ loaders
-    const int lw = warp - 5;  // loader warp: rows [32*lw, 32*lw+32) of each key tile
+    const bool is_v = warp >= 7;                 // warps 5-6: K, warps 7-8: V
+    const int gw = (warp - 5) & 1;               // rows [64*gw, 64*gw+64) of each key tile
+    const __nv_bfloat16* srcb = is_v ? vb : kb;
+    uint8_t* ring = is_v ? sV : sK;
+    uint64_t* full = is_v ? bar_v_full : bar_k_full;
+    uint64_t* empty = is_v ? bar_v_empty : bar_k_empty;
+    const int half = lane >> 4, ch = lane & 15;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      // Source row of key slot 32*lw + lane: binary search of the run table.
-      const int g = j * kTileN + lw * 32 + lane;
-      int src = -1;
-      if (g < total) {
-        int lo2 = 0, hi2 = nsel - 1;  // first run with end > g
-        while (lo2 < hi2) {
-          const int mid = (lo2 + hi2) >> 1;
-          if (s_run_end[mid] > g) hi2 = mid; else lo2 = mid + 1;
+      // Source rows of key slots 64*gw + lane and 64*gw + 32 + lane.
+      int src[2];
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        const int g = j * kTileN + gw * 64 + sub * 32 + lane;
+        src[sub] = -1;
+        if (g < total) {
+          int lo2 = 0, hi2 = nsel - 1;  // first run with end > g
+          while (lo2 < hi2) {
+            const int mid = (lo2 + hi2) >> 1;
+            if (s_run_end[mid] > g) hi2 = mid; else lo2 = mid + 1;
+          }
+          const int prev = lo2 > 0 ? s_run_end[lo2 - 1] : 0;
+          src[sub] = s_run_start[lo2] + (g - prev);
         }
-        const int prev = lo2 > 0 ? s_run_end[lo2 - 1] : 0;
-        src = s_run_start[lo2] + (g - prev);
       }
-      if (j >= 2) mbar_wait(&bar_kv_empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
-      const uint32_t dk = smem_addr(sK + st * kTileBytes), dv = smem_addr(sV + st * kTileBytes);
-      const int half = lane >> 4, ch = lane & 15;
+      if (j >= 2) mbar_wait(&empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
+      const uint32_t dst = smem_addr(ring + st * kTileBytes);
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
 #pragma unroll 4
-      for (int pr = 0; pr < 16; ++pr) {  // two rows per instruction: lanes 0-15 row 2pr, 16-31 row 2pr+1
-        const int rl = 2 * pr + half;
-        const int rsrc = __shfl_sync(0xffffffffu, src, rl);
-        const int r = lw * 32 + rl;
-        const bool ok = rsrc >= 0;
-        const int64_t off = (int64_t)(ok ? rsrc : 0) * kD + ch * 8;
-        const uint32_t o = sw128_off(r, ch, kTileN);
-        cp_async16(dk + o, kb + off, ok);
-        cp_async16(dv + o, vb + off, ok);
+        for (int pr = 0; pr < 16; ++pr) {  // two rows per instruction: lanes 0-15 row 2pr, 16-31 row 2pr+1
+          const int rl = 2 * pr + half;
+          const int rsrc = __shfl_sync(0xffffffffu, src[sub], rl);
+          const int r = gw * 64 + sub * 32 + rl;
+          const bool ok = rsrc >= 0;
+          cp_async16(dst + sw128_off(r, ch, kTileN), srcb + (int64_t)(ok ? rsrc : 0) * kD + ch * 8, ok);
+        }
       }
       cp_async_commit();
       cp_async_wait_all();
       fence_proxy_async_smem();
-      mbar_arrive(&bar_kv_full[st]);
+      mbar_arrive(&full[st]);
     }
   } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
@@ -197,7 +212,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       const uint32_t aq = smem_addr(sQ), ap = smem_addr(sP);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&bar_kv_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) return false;
+        if (!mbar_wait(&bar_k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) return false;
         tc_fence_after();
         const uint32_t bk = smem_addr(sK + st * kTileBytes);
 #pragma unroll
@@ -206,6 +221,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           mma_f16(tS[st], sw128_desc(aq + koff, 16, 1024), sw128_desc(bk + koff, 16, 1024), kIdescQK, kk > 0);
         }
         mma_commit(&bar_s_full[st]);
+        mma_commit(&bar_k_empty[st]);
         return true;
       };
       bool ok = issue_s(0);
@@ -213,6 +229,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j & 1;
         if (!(ok = mbar_wait(&bar_p_full, j & 1, err, kErrTimeoutMma))) break;
+        if (!(ok = mbar_wait(&bar_v_full[st], (j >> 1) & 1, err, kErrTimeoutMma))) break;
         tc_fence_after();
         const uint32_t bv = smem_addr(sV + st * kTileBytes);
 #pragma unroll
@@ -223,7 +240,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
                   (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&bar_o_done);
-        mma_commit(&bar_kv_empty[st]);
+        mma_commit(&bar_v_empty[st]);
         if (j + 2 < ntiles) ok = issue_s(j + 2);
       }
     }

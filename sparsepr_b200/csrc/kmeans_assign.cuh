@@ -8,11 +8,10 @@
 // hi = tf32(v), lo = v - hi and accumulates hi.hi + hi.lo + lo.hi (3xTF32),
 // which reproduces fp32 dot products to ~2^-22 relative.
 //
-// Warp roles (416 threads): warps 0-7 argmin epilogue (warp w reads TMEM
-// lanes 32*(w%4).. and columns 64*(w/4).. of each tile, i.e. two threads per
-// point, merged at the end), warp 8 MMA issuer, warps 9-12 centroid-tile
-// loaders (thread = centroid row: fp32 registers -> swizzled shared memory
-// plus |c|^2, 2-stage ring).  TMEM holds two 128-column
+// Warp roles (288 threads): warps 0-3 argmin epilogue (thread = point = TMEM
+// lane), warp 4 MMA issuer, warps 5-8 centroid-tile loaders (thread =
+// centroid row: fp32 registers -> swizzled shared memory plus |c|^2, 2-stage
+// ring).  TMEM holds two 128-column
 // accumulators so the epilogue of one centroid tile overlaps the next GEMM.
 #pragma once
 #include "tc_common.cuh"
@@ -23,9 +22,8 @@ inline bool assign_supported_dim(int d) { return d >= 4 && d <= 128 && d % 4 == 
 
 constexpr int kAsgM = 128;   // points per CTA
 constexpr int kAsgN = 128;   // centroids per tile
-constexpr int kAsgThreads = 416;
+constexpr int kAsgThreads = 288;
 constexpr int kAsgLoaders = 128;
-constexpr int kAsgEpilogue = 256;
 constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
 
 template <int DP, bool SPLIT>
@@ -91,8 +89,6 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
   __shared__ uint64_t bar_c_full[2], bar_c_empty[2], bar_d_full[2], bar_d_free[2];
   __shared__ uint32_t s_tmem;
   __shared__ float s_csq[2][kAsgN];
-  __shared__ float s_best[kAsgM];
-  __shared__ int s_best_idx[kAsgM];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sx_hi = tc::smem_addr(smem);
   const uint32_t sx_lo = sx_hi + (SPLIT ? L::kXBytes : 0);
@@ -108,11 +104,11 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
       tc::mbar_init(&bar_c_full[i], kAsgLoaders);
       tc::mbar_init(&bar_c_empty[i], 1);
       tc::mbar_init(&bar_d_full[i], 1);
-      tc::mbar_init(&bar_d_free[i], kAsgEpilogue);
+      tc::mbar_init(&bar_d_free[i], 128);
     }
     tc::mbar_fence_init();
   }
-  if (warp == 8) tc::tmem_alloc<256>(&s_tmem);
+  if (warp == 4) tc::tmem_alloc<256>(&s_tmem);
   // Point tile (all threads), zero padding past d and past n.
   const T* xb = x + b * n * d;
   for (int i = tid; i < kAsgM * kChunks; i += kAsgThreads) {
@@ -127,9 +123,9 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp >= 9) {
+  if (warp >= 5) {
     // ---------------------------------------------------------- centroid loaders
-    const int r = tid - 9 * 32;  // centroid row of the tile owned by this thread
+    const int r = tid - 5 * 32;  // centroid row of the tile owned by this thread
     const float* cb = centroids + b * (int64_t)k * d;
     for (int t = 0; t < ntiles; ++t) {
       const int st = t & 1;
@@ -157,7 +153,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
       tc::fence_proxy_async_smem();
       tc::mbar_arrive(&bar_c_full[st]);
     }
-  } else if (warp == 8) {
+  } else if (warp == 4) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       for (int t = 0; t < ntiles; ++t) {
@@ -186,8 +182,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
     }
   } else {
     // ---------------------------------------------------------- argmin epilogue
-    const int row = tid & 127;
-    const int colh = tid >> 7;  // which 64-column half of each tile this thread scans
+    const int row = tid;
     const int64_t p = p0 + row;
     float xsq = 0.f;  // |x|^2 of this point from the staged tile (hi + lo is exact)
 #pragma unroll
@@ -203,9 +198,9 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
       xsq = fmaf(v.z, v.z, xsq);
       xsq = fmaf(v.w, v.w, xsq);
     }
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     float best = 3.4e38f;
-    int best_idx = 0x7fffffff;
+    int best_idx = 0;
     for (int t = 0; t < ntiles; ++t) {
       const int st = t & 1;
       const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[st], (t >> 1) & 1, err, 13));
@@ -213,11 +208,11 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
       tc::tc_fence_after();
       const int k0 = t * kAsgN;
 #pragma unroll 1
-      for (int cb = 2 * colh; cb < 2 * colh + 2; ++cb) {
+      for (int cb = 0; cb < 4; ++cb) {
         float acc[32];
         tc::tmem_ld32(tmem + lane_base + st * 128 + cb * 32, acc);
         // Two interleaved first-minimum chains (even / odd columns) for ILP,
-        // merged with the lower index winning ties.
+        // merged with the lower index winning ties; blocks only increase the index.
         float b0 = 3.4e38f, b1 = 3.4e38f;
         int i0 = 0x7fffffff, i1 = 0x7fffffff;
 #pragma unroll
@@ -229,25 +224,16 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* 
           if (kc + 1 < k && d1 < b1) { b1 = d1; i1 = kc + 1; }
         }
         if (b1 < b0 || (b1 == b0 && i1 < i0)) { b0 = b1; i0 = i1; }
-        if (b0 < best) { best = b0; best_idx = i0; }  // columns only increase across blocks
+        if (b0 < best) { best = b0; best_idx = i0; }
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&bar_d_free[st]);
     }
-    // Merge the two column halves of each point (equal distances: lower index).
-    if (colh == 1) { s_best[row] = best; s_best_idx[row] = best_idx; }
-    tc::named_bar(1, kAsgEpilogue);
-    if (colh == 0) {
-      const float ob = s_best[row];
-      const int oi = s_best_idx[row];
-      if (ob < best || (ob == best && oi < best_idx)) { best = ob; best_idx = oi; }
-      if (best_idx == 0x7fffffff) best_idx = 0;
-      if (p < n) labels[b * n + p] = best_idx;
-    }
+    if (p < n) labels[b * n + p] = best_idx;
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 4) {
     tc::tc_fence_after();
     tc::tmem_dealloc<256>(tmem);
   }
