@@ -168,35 +168,37 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     uint64_t* full = is_v ? bar_v_full : bar_k_full;
     uint64_t* empty = is_v ? bar_v_empty : bar_k_empty;
     const int half = lane >> 4, ch = lane & 15;
+    // Per-lane run cursors: slot g = j*128 + 64*gw + 32*sub + lane grows by 128
+    // per tile, so each cursor only walks forward over the runs it passes.
+    int cur[2] = {0, 0};
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      // Source rows of key slots 64*gw + lane and 64*gw + 32 + lane.
       int src[2];
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {
         const int g = j * kTileN + gw * 64 + sub * 32 + lane;
         src[sub] = -1;
         if (g < total) {
-          int lo2 = 0, hi2 = nsel - 1;  // first run with end > g
-          while (lo2 < hi2) {
-            const int mid = (lo2 + hi2) >> 1;
-            if (s_run_end[mid] > g) hi2 = mid; else lo2 = mid + 1;
-          }
-          const int prev = lo2 > 0 ? s_run_end[lo2 - 1] : 0;
-          src[sub] = s_run_start[lo2] + (g - prev);
+          while (s_run_end[cur[sub]] <= g) ++cur[sub];
+          const int prev = cur[sub] > 0 ? s_run_end[cur[sub] - 1] : 0;
+          src[sub] = s_run_start[cur[sub]] + (g - prev);
         }
       }
       if (j >= 2) mbar_wait(&empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
-      const uint32_t dst = smem_addr(ring + st * kTileBytes);
+      // Swizzled destination of (row r, chunk ch): rows of one warp step differ
+      // only in (r & 7), fixed per unrolled iteration.
+      const uint32_t dst = smem_addr(ring + st * kTileBytes) + (uint32_t)(ch >> 3) * (kTileN * 128) +
+                           (uint32_t)(gw * 64) * 128;
+      const __nv_bfloat16* colp = srcb + ch * 8;
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {
-#pragma unroll 4
+#pragma unroll
         for (int pr = 0; pr < 16; ++pr) {  // two rows per instruction: lanes 0-15 row 2pr, 16-31 row 2pr+1
           const int rl = 2 * pr + half;
           const int rsrc = __shfl_sync(0xffffffffu, src[sub], rl);
-          const int r = gw * 64 + sub * 32 + rl;
-          const bool ok = rsrc >= 0;
-          cp_async16(dst + sw128_off(r, ch, kTileN), srcb + (int64_t)(ok ? rsrc : 0) * kD + ch * 8, ok);
+          const int rr = sub * 32 + rl;  // row within this warp's 64-row band (band start is 8-aligned)
+          const uint32_t o = (uint32_t)rr * 128 + ((uint32_t)((ch & 7) ^ (rr & 7)) << 4);
+          cp_async16(dst + o, colp + (uint32_t)max(rsrc, 0) * (uint32_t)kD, rsrc >= 0);
         }
       }
       cp_async_commit();
@@ -256,30 +258,40 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       if (!ok) break;
       tc_fence_after();
       float s[kTileN];
+      tmem_ld64(tmem + lane_base + st * 128, s);
+      tmem_ld64(tmem + lane_base + st * 128 + 64, s + 64);
+      const int valid = total - j * kTileN;
+      if (valid < kTileN) {  // only the last tile of a cluster is partial (warp-uniform)
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) tmem_ld32(tmem + lane_base + st * 128 + cb * 32, s + cb * 32);
-      const int valid = min(kTileN, total - j * kTileN);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int x = 0; x < kTileN; ++x) {
-        s[x] = x < valid ? s[x] * scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[x]);
+        for (int x = 0; x < kTileN; ++x) s[x] = x < valid ? s[x] : -INFINITY;
       }
+      float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int x = 4; x < kTileN; x += 4) {
+        m4[0] = fmaxf(m4[0], s[x]);
+        m4[1] = fmaxf(m4[1], s[x + 1]);
+        m4[2] = fmaxf(m4[2], s[x + 2]);
+        m4[3] = fmaxf(m4[3], s[x + 3]);
+      }
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
       // Lazy max: keep the running max unless it grew by more than 8 (base 2).
       float alpha = 1.f;
       if (mx > m_run + 8.f || m_run == -INFINITY) {
-        alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mx);
+        alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
         m_run = mx;
       }
-      float sum = 0.f;
+      const float neg_m = -m_run;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kTileN / 2];
 #pragma unroll
       for (int x = 0; x < kTileN; x += 2) {
-        const float p0 = exp2f(s[x] - m_run), p1 = exp2f(s[x + 1] - m_run);
-        sum += p0 + p1;
+        const float p0 = ex2(fmaf(s[x], scale_log2, neg_m));
+        const float p1 = ex2(fmaf(s[x + 1], scale_log2, neg_m));
+        sum4[(x >> 1) & 3] += p0 + p1;
         __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
         pk[x >> 1] = *reinterpret_cast<uint32_t*>(&h);
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       l_run = l_run * alpha + sum;
       if (j > 0) {
         // PV(j-1) must be complete before O is rescaled and P is overwritten.
