@@ -8,11 +8,14 @@
 // hi = tf32(v), lo = v - hi and accumulates hi.hi + hi.lo + lo.hi (3xTF32),
 // which reproduces fp32 dot products to ~2^-22 relative.
 //
-// Warp roles (288 threads): warps 0-3 argmin epilogue (thread = point = TMEM
-// lane), warp 4 MMA issuer, warps 5-8 centroid-tile loaders (thread =
-// centroid row: fp32 registers -> swizzled shared memory plus |c|^2, 2-stage
-// ring).  TMEM holds two 128-column
-// accumulators so the epilogue of one centroid tile overlaps the next GEMM.
+// Persistent kernel: one CTA per SM loops over (problem, 128-point tile)
+// items.  Warp roles (416 threads): warps 0-7 argmin epilogue (warp w reads
+// TMEM lanes 32*(w%4).. and columns 64*(w/4).. of each tile: two threads per
+// point, merged per item), warp 8 MMA issuer, warps 9-12 loaders (thread =
+// row: the point tile of each item into a double buffer, |x|^2, and a
+// continuous stream of centroid tiles with |c|^2 into a 2-stage ring).  TMEM
+// holds two 128-column accumulators so the argmin of one tile overlaps the
+// next GEMM, across item boundaries too.
 #pragma once
 #include "tc_common.cuh"
 
@@ -20,10 +23,11 @@ namespace spr {
 
 inline bool assign_supported_dim(int d) { return d >= 4 && d <= 128 && d % 4 == 0; }
 
-constexpr int kAsgM = 128;   // points per CTA
+constexpr int kAsgM = 128;   // points per item
 constexpr int kAsgN = 128;   // centroids per tile
-constexpr int kAsgThreads = 288;
+constexpr int kAsgThreads = 416;
 constexpr int kAsgLoaders = 128;
+constexpr int kAsgEpilogue = 256;
 constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
 
 template <int DP, bool SPLIT>
@@ -32,7 +36,8 @@ struct AsgSmem {
   static constexpr int kXBytes = kAsgM * kRowBytes;
   static constexpr int kCBytes = kAsgN * kRowBytes;
   static constexpr int kParts = SPLIT ? 2 : 1;
-  static constexpr int kTotal = 1024 + kParts * kXBytes + 2 * kParts * kCBytes;
+  static constexpr int kNX = (1024 + 2 * kParts * kXBytes + 2 * kParts * kCBytes <= 200 * 1024) ? 2 : 1;
+  static constexpr int kTotal = 1024 + kNX * kParts * kXBytes + 2 * kParts * kCBytes;
 };
 
 __device__ __forceinline__ float tf32_hi(float v) {
@@ -81,159 +86,207 @@ __device__ __forceinline__ void put4(uint32_t hi_base, uint32_t lo_base, uint32_
 
 template <int DP, bool SPLIT, typename T>
 __global__ void __launch_bounds__(kAsgThreads, 1)
-assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, const float* __restrict__ centroids,
+assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items, const float* __restrict__ centroids,
                  int32_t* __restrict__ labels, const int* __restrict__ done, int* __restrict__ err) {
   using L = AsgSmem<DP, SPLIT>;
+  constexpr int NX = L::kNX;
+  constexpr int kChunks = DP / 4;  // 16-byte chunks per row
   if (done && *done) return;
   extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_x_full[2], bar_x_empty[2], bar_x_read[2];
   __shared__ uint64_t bar_c_full[2], bar_c_empty[2], bar_d_full[2], bar_d_free[2];
   __shared__ uint32_t s_tmem;
   __shared__ float s_csq[2][kAsgN];
+  __shared__ float s_xsq[2][kAsgM];
+  __shared__ float s_best[kAsgM];
+  __shared__ int s_best_idx[kAsgM];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sx_hi = tc::smem_addr(smem);
-  const uint32_t sx_lo = sx_hi + (SPLIT ? L::kXBytes : 0);
-  const uint32_t sc0 = sx_hi + L::kParts * L::kXBytes;  // stage s: hi at sc0 + s*parts*C, lo after hi
-  const int64_t b = blockIdx.y;
-  const int64_t p0 = (int64_t)blockIdx.x * kAsgM;
+  const uint32_t sx0 = tc::smem_addr(smem);                       // X buffer i: hi at sx0 + i*parts*X
+  const uint32_t sc0 = sx0 + NX * L::kParts * L::kXBytes;         // C stage s: hi at sc0 + s*parts*C
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ntiles = (k + kAsgN - 1) / kAsgN;
-  constexpr int kChunks = DP / 4;  // 16-byte chunks per row
+  const int ctiles = (k + kAsgN - 1) / kAsgN;
+  const int64_t ptiles = (n + kAsgM - 1) / kAsgM;
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_x_full[i], kAsgLoaders);
+      tc::mbar_init(&bar_x_empty[i], 1);
+      tc::mbar_init(&bar_x_read[i], kAsgEpilogue);
       tc::mbar_init(&bar_c_full[i], kAsgLoaders);
       tc::mbar_init(&bar_c_empty[i], 1);
       tc::mbar_init(&bar_d_full[i], 1);
-      tc::mbar_init(&bar_d_free[i], 128);
+      tc::mbar_init(&bar_d_free[i], kAsgEpilogue);
     }
     tc::mbar_fence_init();
   }
-  if (warp == 4) tc::tmem_alloc<256>(&s_tmem);
-  // Point tile (all threads), zero padding past d and past n.
-  const T* xb = x + b * n * d;
-  for (int i = tid; i < kAsgM * kChunks; i += kAsgThreads) {
-    const int r = i / kChunks, ch = i % kChunks;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p0 + r < n && ch * 4 < d) v = load4<T>(xb + (p0 + r) * d + ch * 4);
-    put4<SPLIT>(sx_hi, sx_lo, tc::sw128_off(r, ch, kAsgM), v);
-  }
-  tc::fence_proxy_async_smem();
+  if (warp == 8) tc::tmem_alloc<256>(&s_tmem);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  if (warp >= 5) {
-    // ---------------------------------------------------------- centroid loaders
-    const int r = tid - 5 * 32;  // centroid row of the tile owned by this thread
-    const float* cb = centroids + b * (int64_t)k * d;
-    for (int t = 0; t < ntiles; ++t) {
-      const int st = t & 1;
-      const int kc = t * kAsgN + r;
-      float4 v[kChunks];
-      float sq = 0.f;
+  if (warp >= 9) {
+    // ---------------------------------------------------------- loaders (thread = row)
+    const int r = tid - 9 * 32;
+    int64_t gt = 0;  // global centroid-tile counter of this CTA
+    int il = 0;      // item counter of this CTA
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++il) {
+      const int64_t b = it / ptiles;
+      const int64_t p0 = (it % ptiles) * kAsgM;
+      // Point tile: row r of this item, and its |x|^2 from the values stored.
+      {
+        const int xb = il % NX;
+        if (il >= NX) {
+          tc::mbar_wait(&bar_x_empty[xb], ((il / NX) - 1) & 1, err, 21);
+          tc::mbar_wait(&bar_x_read[xb], ((il / NX) - 1) & 1, err, 21);
+        }
+        const uint32_t hi = sx0 + xb * L::kParts * L::kXBytes;
+        const uint32_t lo = hi + (SPLIT ? L::kXBytes : 0);
+        const T* xr = x + (b * n + p0 + r) * d;
+        const bool row_ok = p0 + r < n;
+        float sq = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < kChunks; ++ch) {
-        v[ch] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kc < k && ch * 4 < d) v[ch] = *reinterpret_cast<const float4*>(cb + (int64_t)kc * d + ch * 4);
-        sq = fmaf(v[ch].x, v[ch].x, sq);
-        sq = fmaf(v[ch].y, v[ch].y, sq);
-        sq = fmaf(v[ch].z, v[ch].z, sq);
-        sq = fmaf(v[ch].w, v[ch].w, sq);
+        for (int ch = 0; ch < kChunks; ++ch) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (row_ok && ch * 4 < d) v = load4<T>(xr + ch * 4);
+          sq = fmaf(v.x, v.x, sq);
+          sq = fmaf(v.y, v.y, sq);
+          sq = fmaf(v.z, v.z, sq);
+          sq = fmaf(v.w, v.w, sq);
+          put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgM), v);
+        }
+        s_xsq[xb][r] = sq;
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&bar_x_full[xb]);
       }
-      if (t >= 2) {  // the GEMM and the argmin of tile t-2 are both done with this stage
-        tc::mbar_wait(&bar_c_empty[st], ((t >> 1) - 1) & 1, err, 11);
-        tc::mbar_wait(&bar_d_free[st], ((t >> 1) - 1) & 1, err, 11);
-      }
-      const uint32_t hi = sc0 + st * L::kParts * L::kCBytes;
-      const uint32_t lo = hi + (SPLIT ? L::kCBytes : 0);
+      const float* cb = centroids + b * (int64_t)k * d;
+      for (int t = 0; t < ctiles; ++t, ++gt) {
+        const int st = (int)(gt & 1);
+        const int kc = t * kAsgN + r;
+        float4 v[kChunks];
+        float sq = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < kChunks; ++ch) put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgN), v[ch]);
-      s_csq[st][r] = sq;
-      tc::fence_proxy_async_smem();
-      tc::mbar_arrive(&bar_c_full[st]);
+        for (int ch = 0; ch < kChunks; ++ch) {
+          v[ch] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (kc < k && ch * 4 < d) v[ch] = *reinterpret_cast<const float4*>(cb + (int64_t)kc * d + ch * 4);
+          sq = fmaf(v[ch].x, v[ch].x, sq);
+          sq = fmaf(v[ch].y, v[ch].y, sq);
+          sq = fmaf(v[ch].z, v[ch].z, sq);
+          sq = fmaf(v[ch].w, v[ch].w, sq);
+        }
+        if (gt >= 2) {  // the GEMM and the argmin of tile gt-2 are both done with this stage
+          tc::mbar_wait(&bar_c_empty[st], (int)(((gt >> 1) - 1) & 1), err, 11);
+          tc::mbar_wait(&bar_d_free[st], (int)(((gt >> 1) - 1) & 1), err, 11);
+        }
+        const uint32_t hi = sc0 + st * L::kParts * L::kCBytes;
+        const uint32_t lo = hi + (SPLIT ? L::kCBytes : 0);
+#pragma unroll
+        for (int ch = 0; ch < kChunks; ++ch) put4<SPLIT>(hi, lo, tc::sw128_off(r, ch, kAsgN), v[ch]);
+        s_csq[st][r] = sq;
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&bar_c_full[st]);
+      }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      for (int t = 0; t < ntiles; ++t) {
-        const int st = t & 1;
-        if (!tc::mbar_wait(&bar_c_full[st], (t >> 1) & 1, err, 12)) break;
-        if (t >= 2 && !tc::mbar_wait(&bar_d_free[st], ((t >> 1) - 1) & 1, err, 12)) break;
-        tc::tc_fence_after();
-        const uint32_t chi = sc0 + st * L::kParts * L::kCBytes;
-        const uint32_t clo = chi + (SPLIT ? L::kCBytes : 0);
-        const uint32_t dt = tmem + st * 128;
+      int64_t gt = 0;
+      int il = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; ok && it < items; it += gridDim.x, ++il) {
+        const int xb = il % NX;
+        if (!(ok = tc::mbar_wait(&bar_x_full[xb], (il / NX) & 1, err, 12))) break;
+        const uint32_t xhi = sx0 + xb * L::kParts * L::kXBytes;
+        const uint32_t xlo = xhi + (SPLIT ? L::kXBytes : 0);
+        for (int t = 0; t < ctiles; ++t, ++gt) {
+          const int st = (int)(gt & 1);
+          if (!(ok = tc::mbar_wait(&bar_c_full[st], (int)((gt >> 1) & 1), err, 12))) break;
+          if (gt >= 2 && !(ok = tc::mbar_wait(&bar_d_free[st], (int)(((gt >> 1) - 1) & 1), err, 12))) break;
+          tc::tc_fence_after();
+          const uint32_t chi = sc0 + st * L::kParts * L::kCBytes;
+          const uint32_t clo = chi + (SPLIT ? L::kCBytes : 0);
+          const uint32_t dt = tmem + st * 128;
 #pragma unroll
-        for (int kk = 0; kk < DP / 8; ++kk) {  // 8 tf32 = 32 bytes per MMA K step
-          const uint32_t kb = kk * 32;
-          const uint32_t oa = (kb >> 7) * (kAsgM * 128) + (kb & 127);
-          const uint32_t ob = (kb >> 7) * (kAsgN * 128) + (kb & 127);
-          tc::mma_tf32(dt, tc::sw128_desc(sx_hi + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg,
-                       kk > 0);
-          if constexpr (SPLIT) {
-            tc::mma_tf32(dt, tc::sw128_desc(sx_hi + oa, 16, 1024), tc::sw128_desc(clo + ob, 16, 1024), kIdescAsg, 1);
-            tc::mma_tf32(dt, tc::sw128_desc(sx_lo + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg, 1);
+          for (int kk = 0; kk < DP / 8; ++kk) {  // 8 tf32 = 32 bytes per MMA K step
+            const uint32_t kb = kk * 32;
+            const uint32_t oa = (kb >> 7) * (kAsgM * 128) + (kb & 127);
+            const uint32_t ob = (kb >> 7) * (kAsgN * 128) + (kb & 127);
+            tc::mma_tf32(dt, tc::sw128_desc(xhi + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg,
+                         kk > 0);
+            if constexpr (SPLIT) {
+              tc::mma_tf32(dt, tc::sw128_desc(xhi + oa, 16, 1024), tc::sw128_desc(clo + ob, 16, 1024), kIdescAsg, 1);
+              tc::mma_tf32(dt, tc::sw128_desc(xlo + oa, 16, 1024), tc::sw128_desc(chi + ob, 16, 1024), kIdescAsg, 1);
+            }
           }
+          tc::mma_commit(&bar_d_full[st]);
+          tc::mma_commit(&bar_c_empty[st]);
+          if (t == ctiles - 1) tc::mma_commit(&bar_x_empty[xb]);
         }
-        tc::mma_commit(&bar_d_full[st]);
-        tc::mma_commit(&bar_c_empty[st]);
       }
     }
   } else {
     // ---------------------------------------------------------- argmin epilogue
-    const int row = tid;
-    const int64_t p = p0 + row;
-    float xsq = 0.f;  // |x|^2 of this point from the staged tile (hi + lo is exact)
-#pragma unroll
-    for (int ch = 0; ch < kChunks; ++ch) {
-      float4 h, l = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t off = tc::sw128_off(row, ch, kAsgM);
-      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(h.x), "=f"(h.y), "=f"(h.z), "=f"(h.w) : "r"(sx_hi + off));
-      if constexpr (SPLIT)
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l.x), "=f"(l.y), "=f"(l.z), "=f"(l.w) : "r"(sx_lo + off));
-      const float4 v = make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
-      xsq = fmaf(v.x, v.x, xsq);
-      xsq = fmaf(v.y, v.y, xsq);
-      xsq = fmaf(v.z, v.z, xsq);
-      xsq = fmaf(v.w, v.w, xsq);
-    }
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    float best = 3.4e38f;
-    int best_idx = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      const int st = t & 1;
-      const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[st], (t >> 1) & 1, err, 13));
-      if (!ok) break;
-      tc::tc_fence_after();
-      const int k0 = t * kAsgN;
+    const int row = tid & 127;
+    const int colh = tid >> 7;  // 64-column half of each tile scanned by this thread
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    int64_t gt = 0;
+    int il = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++il) {
+      const int64_t b = it / ptiles;
+      const int64_t p = (it % ptiles) * kAsgM + row;
+      const int xb = il % NX;
+      ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_x_full[xb], (il / NX) & 1, err, 13));
+      const float xsq = s_xsq[xb][row];
+      tc::mbar_arrive(&bar_x_read[xb]);
+      float best = 3.4e38f;
+      int best_idx = 0x7fffffff;
+      for (int t = 0; t < ctiles; ++t, ++gt) {
+        const int st = (int)(gt & 1);
+        ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[st], (int)((gt >> 1) & 1), err, 13));
+        tc::tc_fence_after();
+        const int k0 = t * kAsgN;
+        if (ok) {
 #pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
-        float acc[32];
-        tc::tmem_ld32(tmem + lane_base + st * 128 + cb * 32, acc);
-        // Two interleaved first-minimum chains (even / odd columns) for ILP,
-        // merged with the lower index winning ties; blocks only increase the index.
-        float b0 = 3.4e38f, b1 = 3.4e38f;
-        int i0 = 0x7fffffff, i1 = 0x7fffffff;
+          for (int cb = 2 * colh; cb < 2 * colh + 2; ++cb) {
+            float acc[32];
+            tc::tmem_ld32(tmem + lane_base + st * 128 + cb * 32, acc);
+            // Two interleaved first-minimum chains (even / odd columns), merged
+            // with the lower index winning ties; blocks only increase the index.
+            float b0 = 3.4e38f, b1 = 3.4e38f;
+            int i0 = 0x7fffffff, i1 = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int kc = k0 + cb * 32 + j;
-          const float d0 = fmaxf(xsq + s_csq[st][cb * 32 + j] - 2.f * acc[j], 0.f);
-          const float d1 = fmaxf(xsq + s_csq[st][cb * 32 + j + 1] - 2.f * acc[j + 1], 0.f);
-          if (kc < k && d0 < b0) { b0 = d0; i0 = kc; }
-          if (kc + 1 < k && d1 < b1) { b1 = d1; i1 = kc + 1; }
+            for (int j = 0; j < 32; j += 2) {
+              const int kc = k0 + cb * 32 + j;
+              const float2 c2 = *reinterpret_cast<const float2*>(&s_csq[st][cb * 32 + j]);
+              const float d0 = fmaxf(fmaf(-2.f, acc[j], xsq + c2.x), 0.f);
+              const float d1 = fmaxf(fmaf(-2.f, acc[j + 1], xsq + c2.y), 0.f);
+              if (kc < k && d0 < b0) { b0 = d0; i0 = kc; }
+              if (kc + 1 < k && d1 < b1) { b1 = d1; i1 = kc + 1; }
+            }
+            if (b1 < b0 || (b1 == b0 && i1 < i0)) { b0 = b1; i0 = i1; }
+            if (b0 < best) { best = b0; best_idx = i0; }
+          }
         }
-        if (b1 < b0 || (b1 == b0 && i1 < i0)) { b0 = b1; i0 = i1; }
-        if (b0 < best) { best = b0; best_idx = i0; }
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bar_d_free[st]);
       }
-      tc::tc_fence_before();
-      tc::mbar_arrive(&bar_d_free[st]);
+      // Merge the two column halves of each point (equal distances: lower index).
+      if (colh == 1) { s_best[row] = best; s_best_idx[row] = best_idx; }
+      tc::named_bar(1, kAsgEpilogue);
+      if (colh == 0) {
+        const float ob = s_best[row];
+        const int oi = s_best_idx[row];
+        if (ob < best || (ob == best && oi < best_idx)) { best = ob; best_idx = oi; }
+        if (best_idx == 0x7fffffff) best_idx = 0;
+        if (p < n) labels[b * n + p] = best_idx;
+      }
+      tc::named_bar(1, kAsgEpilogue);
     }
-    if (p < n) labels[b * n + p] = best_idx;
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc::tc_fence_after();
     tc::tmem_dealloc<256>(tmem);
   }
@@ -245,8 +298,12 @@ static int launch_assign_tc(const void* x, int64_t bh, int64_t n, int d, int k, 
   constexpr int smem = AsgSmem<DP, SPLIT>::kTotal;
   auto kern = assign_tc_kernel<DP, SPLIT, T>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  dim3 grid((unsigned)((n + kAsgM - 1) / kAsgM), (unsigned)bh);
-  kern<<<grid, kAsgThreads, smem, st>>>((const T*)x, n, d, k, c, labels, done, err);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t items = bh * ((n + kAsgM - 1) / kAsgM);
+  const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
+  kern<<<grid, kAsgThreads, smem, st>>>((const T*)x, n, d, k, items, c, labels, done, err);
   return check_launch("k-means assign (tcgen05)");
 }
 
