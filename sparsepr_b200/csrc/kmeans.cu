@@ -309,11 +309,19 @@ static int seg_mean_dispatch(int x_dtype, const void* x, const int32_t* order, c
   return fail(SPR_ERR_DTYPE, "segmented mean: unsupported dtype %d", x_dtype);
 }
 
+static int check_kmeans_alignment(const void* x, const float* centroids) {
+  // Rows are read with 8/16-byte vector loads (d is a multiple of 4).
+  if (!aligned(x, 16) || !aligned(centroids, 16))
+    return fail(SPR_ERR_ALIGN, "k-means: x and centroids must be 16-byte aligned");
+  return SPR_OK;
+}
+
 extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k,
                                  const float* centroids, int precision, int32_t* labels, void* workspace,
                                  size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
+  if ((s = check_kmeans_alignment(x, centroids))) return s;
   if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
     return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);
   Carver c(workspace, workspace_bytes);
@@ -341,6 +349,7 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
                                 void* workspace, size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
+  if ((s = check_kmeans_alignment(x, centroids))) return s;
   if (iters < 1 || iters > 1024) return fail(SPR_ERR_ARG, "k-means: iters=%d must be in [1,1024]", iters);
   if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
     return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);

@@ -96,7 +96,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
   __shared__ uint64_t bar_x_full[2], bar_x_empty[2], bar_x_read[2];
   __shared__ uint64_t bar_c_full[2], bar_c_empty[2], bar_d_full[2], bar_d_free[2];
   __shared__ uint32_t s_tmem;
-  __shared__ float s_csq[2][kAsgN];
+  __shared__ __align__(16) float s_csq[2][kAsgN];  // read as float2 by the epilogue
   __shared__ float s_xsq[2][kAsgM];
   __shared__ float s_best[kAsgM];
   __shared__ int s_best_idx[kAsgM];
