@@ -201,11 +201,9 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           cp_async16(dst + o, colp + (uint32_t)max(rsrc, 0) * (uint32_t)kD, rsrc >= 0);
         }
       }
-      cp_async_commit();
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&full[st]);
+      cp_async_arrive(&full[st]);  // completes when this lane's copies have landed
     }
+    cp_async_wait_all();
   } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && ntiles > 0) {

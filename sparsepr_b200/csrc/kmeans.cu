@@ -230,6 +230,7 @@ struct KmeansWs {
   int* done;         // convergence flag
   float* shifts;     // per-iteration max centroid shift
   float* csq;        // |c|^2 per centroid
+  float* xsq;        // |x|^2 per point (fp32 points)
   int32_t* counts;   // per-(cluster, chunk) counts / starts of the label sort
   float* next;       // updated centroids
 };
@@ -240,6 +241,7 @@ static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
   w.done = c.take<int>(4);
   w.shifts = c.take<float>(1024);
   w.csq = c.take<float>((size_t)bh * k);
+  w.xsq = c.take<float>((size_t)bh * n);
   w.counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
   w.next = c.take<float>((size_t)bh * k * d);
   return w;
@@ -329,7 +331,8 @@ extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t
   if (!c.ok() || !workspace) return fail(SPR_ERR_WORKSPACE, "k-means assign: workspace %zu < %zu", workspace_bytes, c.off);
   cudaStream_t st = (cudaStream_t)stream;
   cudaMemsetAsync(w.err, 0, sizeof(int), st);
-  return launch_assign(x, x_dtype, bh, n, d, k, centroids, precision, labels, nullptr, w.err, st);
+  if ((s = launch_point_sq(x, x_dtype, bh, n, d, w.xsq, st))) return s;
+  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.csq, precision, labels, nullptr, w.err, st);
 }
 
 extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
@@ -365,8 +368,9 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
   cudaMemsetAsync(w.err, 0, (size_t)((char*)(w.shifts + 1024) - (char*)w.err), st);
   cudaMemsetAsync(iters_done, 0, sizeof(int32_t), st);
   const int64_t count = bh * k * (int64_t)d;
+  if ((s = launch_point_sq(x, x_dtype, bh, n, d, w.xsq, st))) return s;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, precision, labels, done, w.err, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.csq, precision, labels, done, w.err, st))) return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))
