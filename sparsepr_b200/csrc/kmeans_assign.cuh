@@ -118,7 +118,9 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
   if (done && *done) return;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_x_full[2], bar_x_empty[2], bar_x_read[2];
-  __shared__ uint64_t bar_c_full[NC], bar_c_empty[NC], bar_d_full[2], bar_d_free[2];
+  // c_read[s]: the argmin warps are done with |c|^2 of stage s (one completion
+  // per stage use, so a parity wait on it can never alias a later use).
+  __shared__ uint64_t bar_c_full[NC], bar_c_empty[NC], bar_c_read[NC], bar_d_full[2], bar_d_free[2];
   __shared__ uint32_t s_tmem;
   __shared__ __align__(16) float s_csq[NC][kAsgN];  // read as float2 by the epilogue
   __shared__ __align__(16) float s_xsq[2][kAsgM];
@@ -142,6 +144,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
     for (int i = 0; i < NC; ++i) {
       tc::mbar_init(&bar_c_full[i], kAsgLoaders);
       tc::mbar_init(&bar_c_empty[i], 1);
+      tc::mbar_init(&bar_c_read[i], kAsgEpilogue);
     }
     tc::mbar_fence_init();
   }
@@ -204,7 +207,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
         if constexpr (kAsync) {
           if (gt >= NC) {  // the GEMM and the argmin of tile gt-NC are both done with this stage
             tc::mbar_wait(&bar_c_empty[st], (use - 1) & 1, err, 11);
-            tc::mbar_wait(&bar_d_free[(gt - NC) & 1], (int)(((gt - NC) >> 1) & 1), err, 11);
+            tc::mbar_wait(&bar_c_read[st], (use - 1) & 1, err, 11);
           }
           const int k0 = t * kAsgN;
           for (int idx = r; idx < kAsgN * kChunks; idx += kAsgLoaders) {
@@ -232,7 +235,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
           }
           if (gt >= NC) {
             tc::mbar_wait(&bar_c_empty[st], (use - 1) & 1, err, 11);
-            tc::mbar_wait(&bar_d_free[(gt - NC) & 1], (int)(((gt - NC) >> 1) & 1), err, 11);
+            tc::mbar_wait(&bar_c_read[st], (use - 1) & 1, err, 11);
           }
           const uint32_t lo = hi + (SPLIT ? L::kCBytes : 0);
 #pragma unroll
@@ -329,6 +332,7 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
         }
         tc::tc_fence_before();
         tc::mbar_arrive(&bar_d_free[st]);
+        tc::mbar_arrive(&bar_c_read[cs]);
       }
       // Merge the two column halves of each point (equal distances: lower index).
       if (colh == 1) { s_best[row] = best; s_best_idx[row] = best_idx; }

@@ -44,9 +44,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0 && globaltimer() - t0 > limit_ns) {
-      if (err) atomicCAS(err, 0, code);
-      return false;
+    if ((++spins & 255u) == 0) {
+      // Another wait of this launch already gave up: stop waiting too, so a
+      // stuck pipeline ends in ~limit_ns instead of one timeout per wait.
+      if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (globaltimer() - t0 > limit_ns) {
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
     }
   }
   return true;

@@ -175,3 +175,19 @@ def test_sym_eig_matches_lapack(cuda, n):
     eye = torch.eye(n, dtype=torch.float64)
     assert (v.transpose(1, 2) @ v - eye).abs().max().item() < 1e-4
     assert torch.all(w[:, 1:] >= w[:, :-1])
+
+
+@pytest.mark.parametrize("precision", ["tf32", "fp32"])
+def test_assign_many_items_per_cta(cuda, precision):
+    """Persistent assignment with many point tiles per CTA and 8 centroid tiles
+    (the config-3 K-role shape class) completes, reports no device error and
+    agrees with the oracle away from near ties."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(6, 30000, 48, generator=g)
+    c = torch.randn(6, 1000, 48, generator=g)
+    got = K.kmeans_assign(x.to(cuda), c.to(cuda), precision)
+    assert K.kmeans_error_code(cuda) == 0
+    ref = oracle.euclid_assign(x, c)
+    rel = 1e-5 if precision == "fp32" else 4e-3
+    ok = _near_tie_free(x, c, rel)
+    assert torch.equal(got.cpu().long()[ok], ref[ok])
