@@ -198,3 +198,18 @@ def test_warm_second_call_runs(cuda):
     assert torch.isfinite(out2.float()).all()
     # A warm call re-clusters from the previous centroids: a nearby, not identical, route.
     assert torch.nn.functional.cosine_similarity(out1.float().flatten(), out2.float().flatten(), dim=0) > 0.9
+
+
+def test_graph_replay_matches_eager(cuda):
+    """The captured layer replays the same kernels: same output as an eager call."""
+    from sparsepr_b200.graph import GraphedSparseAttention
+
+    cfg = _cfg()
+    q, k, v = (t.to(cuda) for t in synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16))
+    eager, _, _ = sparse_attention(q, k, v, N8V6Core(cfg))
+    g = GraphedSparseAttention(q.shape, cfg, cuda).capture()
+    got = g(q, k, v).clone()
+    again = g(q, k, v).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(got, again)
+    _close(got.view(2, -1, 128), eager.view(2, -1, 128))
