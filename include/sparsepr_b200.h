@@ -195,6 +195,15 @@ int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_perm, const 
 int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
                 void* stream);
 
+/*
+ * Batched Cholesky solve A x = b of symmetric positive definite systems:
+ * a [batch,m,m] fp32 (m <= 128), b and x [batch,m,nrhs] fp32 (x must not alias b).
+ * A system that is not positive definite yields non-finite x (no error, no trap).
+ * Replaces the torch.linalg.cholesky_ex + cholesky_solve dual ridge solve of
+ * src/sparsepr/models/cosmos3/residual_repair.py:389-404.
+ */
+int spr_chol_solve(const float* a, const float* b, int64_t batch, int m, int nrhs, float* x, void* stream);
+
 /* ---------------------------------------------------------------- repair */
 
 /*

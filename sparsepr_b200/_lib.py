@@ -43,6 +43,7 @@ PROTOTYPES = {
     "spr_block_sparse_attn_workspace_bytes": (_SZ, [_I64, _I64, _I]),
     "spr_block_sparse_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]),
     "spr_sym_eig": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "spr_chol_solve": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "spr_repair_apply": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _I, _P, _P]),
 }
 

@@ -269,3 +269,15 @@ def sym_eig(a: torch.Tensor, max_sweeps: int = 15):
     _count(1)
     _lib.call("spr_sym_eig", _p(a), b, n, int(max_sweeps), _p(evals), _p(evecs), _stream(dev))
     return evals, evecs
+
+
+def chol_solve(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Solve A X = B for batched SPD A [B,m,m] and B [B,m,r] (fp32); non-PD A gives non-finite X."""
+    dev = _cuda(a, b)
+    bt, m, _ = a.shape
+    a = a.to(torch.float32).contiguous()
+    b = b.to(torch.float32).contiguous()
+    x = torch.empty_like(b)
+    _count(1)
+    _lib.call("spr_chol_solve", _p(a), _p(b), bt, m, b.shape[2], _p(x), _stream(dev))
+    return x

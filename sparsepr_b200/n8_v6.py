@@ -328,8 +328,7 @@ def fit_reduced_rank_residual(x_fit, y_fit, weights, rank: int, ridge: float):
         raise RuntimeError("The dual RRR fit needs fewer probe rows than features.")
     gram = torch.bmm(xw, xw.transpose(1, 2))
     gram.diagonal(dim1=1, dim2=2).add_(float(ridge))
-    chol, _info = torch.linalg.cholesky_ex(gram, check_errors=False)
-    dual = torch.cholesky_solve(yw, chol)
+    dual = K.chol_solve(gram, yw)
     evals, evecs = K.sym_eig(torch.bmm(yw, yw.transpose(1, 2)))
     evecs = evecs[:, :, -rank:]
     scales = evals[:, -rank:].clamp_min(1e-20).rsqrt().unsqueeze(1)

@@ -191,3 +191,16 @@ def test_assign_many_items_per_cta(cuda, precision):
     rel = 1e-5 if precision == "fp32" else 4e-3
     ok = _near_tie_free(x, c, rel)
     assert torch.equal(got.cpu().long()[ok], ref[ok])
+
+
+@pytest.mark.parametrize("m,r", [(64, 128), (16, 64), (128, 3)])
+def test_chol_solve_matches_lapack(cuda, m, r):
+    g = torch.Generator().manual_seed(m)
+    x = torch.randn(3, m, 2 * m, generator=g)
+    a = x @ x.transpose(1, 2) / (2 * m) + 0.1 * torch.eye(m)
+    b = torch.randn(3, m, r, generator=g)
+    ref = torch.linalg.solve(a.double(), b.double())
+    got = K.chol_solve(a.to(cuda), b.to(cuda)).cpu().double()
+    assert ((got - ref).abs().max() / ref.abs().max()).item() < 1e-4
+    bad = -torch.eye(m).expand(1, m, m)  # not positive definite: non-finite, no error
+    assert not torch.isfinite(K.chol_solve(bad.to(cuda), b[:1].to(cuda))).all()
