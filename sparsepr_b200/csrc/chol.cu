@@ -65,6 +65,7 @@ extern "C" int spr_chol_solve(const float* a, const float* b, int64_t batch, int
                 (long long)batch, m, nrhs);
   if (x == b) return fail(SPR_ERR_ARG, "chol_solve: x must not alias b");
   const int smem = m * kCholLd * (int)sizeof(float);
+  cudaFuncSetAttribute(chol_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCholMax * kCholLd * 4);
   chol_solve_kernel<<<(unsigned)batch, 256, smem, (cudaStream_t)stream>>>(a, b, m, nrhs, x);
   return check_launch("chol_solve");
 }
