@@ -309,25 +309,42 @@ assign_tc_kernel(const T* __restrict__ x, int64_t n, int d, int k, int64_t items
         tc::tc_fence_after();
         const int k0 = t * kAsgN;
         if (ok) {
+          // dist = max(|x|^2 + |c|^2 - 2 x.c, 0) is compared as
+          // t = max(|c|^2 - 2 x.c, -|x|^2): the same order and the same
+          // clamp, one FFMA + one FMNMX per column.
+          const float floor_t = -xsq;
+          const bool full = k0 + kAsgN <= k;  // only the last centroid tile is partial
 #pragma unroll 1
           for (int cb = 2 * colh; cb < 2 * colh + 2; ++cb) {
             float acc[32];
             tc::tmem_ld32(tmem + lane_base + st * 128 + cb * 32, acc);
-            // Two interleaved first-minimum chains (even / odd columns), merged
-            // with the lower index winning ties; blocks only increase the index.
+            const float* cq = &s_csq[cs][cb * 32];
+            // Two interleaved first-minimum chains (even / odd columns) with
+            // column offsets as immediates; merged with the lower index on ties.
             float b0 = 3.4e38f, b1 = 3.4e38f;
-            int i0 = 0x7fffffff, i1 = 0x7fffffff;
+            int j0 = 0, j1 = 1;
+            if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const int kc = k0 + cb * 32 + j;
-              const float2 c2 = *reinterpret_cast<const float2*>(&s_csq[cs][cb * 32 + j]);
-              const float d0 = fmaxf(fmaf(-2.f, acc[j], xsq + c2.x), 0.f);
-              const float d1 = fmaxf(fmaf(-2.f, acc[j + 1], xsq + c2.y), 0.f);
-              if (kc < k && d0 < b0) { b0 = d0; i0 = kc; }
-              if (kc + 1 < k && d1 < b1) { b1 = d1; i1 = kc + 1; }
+              for (int j = 0; j < 32; j += 2) {
+                const float2 c2 = *reinterpret_cast<const float2*>(cq + j);
+                const float t0 = fmaxf(fmaf(-2.f, acc[j], c2.x), floor_t);
+                const float t1 = fmaxf(fmaf(-2.f, acc[j + 1], c2.y), floor_t);
+                if (t0 < b0) { b0 = t0; j0 = j; }
+                if (t1 < b1) { b1 = t1; j1 = j + 1; }
+              }
+            } else {
+              const int lim = k - (k0 + cb * 32);  // valid columns in this block (may be <= 0)
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                const float2 c2 = *reinterpret_cast<const float2*>(cq + j);
+                const float t0 = fmaxf(fmaf(-2.f, acc[j], c2.x), floor_t);
+                const float t1 = fmaxf(fmaf(-2.f, acc[j + 1], c2.y), floor_t);
+                if (j < lim && t0 < b0) { b0 = t0; j0 = j; }
+                if (j + 1 < lim && t1 < b1) { b1 = t1; j1 = j + 1; }
+              }
             }
-            if (b1 < b0 || (b1 == b0 && i1 < i0)) { b0 = b1; i0 = i1; }
-            if (b0 < best) { best = b0; best_idx = i0; }
+            if (b1 < b0 || (b1 == b0 && j1 < j0)) { b0 = b1; j0 = j1; }
+            if (b0 < best) { best = b0; best_idx = k0 + cb * 32 + j0; }
           }
         }
         tc::tc_fence_before();
