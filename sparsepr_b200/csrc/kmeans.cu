@@ -229,8 +229,10 @@ struct KmeansWs {
   int* err;          // device status word of the last call (0 = ok)
   int* done;         // convergence flag
   float* shifts;     // per-iteration max centroid shift
-  float* csq;        // |c|^2 per centroid
-  float* xsq;        // |x|^2 per point (fp32 points)
+  float* csq;        // |c|^2 per centroid (padded to whole 128-centroid tiles)
+  float* xsq;        // |x|^2 per point (fp32 points, register path)
+  float* xmax;       // max |x|^2 per problem (TMA path)
+  float* bias;       // (B, base) per problem, then centroid-norm scratch (TMA path)
   int32_t* counts;   // per-(cluster, chunk) counts / starts of the label sort
   float* next;       // updated centroids
 };
@@ -240,8 +242,11 @@ static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
   w.err = c.take<int>(16);
   w.done = c.take<int>(4);
   w.shifts = c.take<float>(1024);
-  w.csq = c.take<float>((size_t)bh * k);
+  w.csq = c.take<float>(centroid_sq_pad_count(bh, k));
   w.xsq = c.take<float>((size_t)bh * n);
+  // xmax and bias are contiguous (5 * bh floats, cleared by one memset).
+  w.xmax = c.take<float>((size_t)bh * 5);
+  w.bias = w.xmax + bh;
   w.counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
   w.next = c.take<float>((size_t)bh * k * d);
   return w;
@@ -311,10 +316,12 @@ static int seg_mean_dispatch(int x_dtype, const void* x, const int32_t* order, c
   return fail(SPR_ERR_DTYPE, "segmented mean: unsupported dtype %d", x_dtype);
 }
 
-static int check_kmeans_alignment(const void* x, const float* centroids) {
-  // Rows are read with 8/16-byte vector loads (d is a multiple of 4).
+static int check_kmeans_alignment(const void* x, const float* centroids, const void* workspace) {
+  // Rows are read with 8/16-byte vector loads or TMA (d is a multiple of 4);
+  // the workspace's |c|^2 tiles are bulk-copied.
   if (!aligned(x, 16) || !aligned(centroids, 16))
     return fail(SPR_ERR_ALIGN, "k-means: x and centroids must be 16-byte aligned");
+  if (!aligned(workspace, 16)) return fail(SPR_ERR_ALIGN, "k-means: workspace must be 16-byte aligned");
   return SPR_OK;
 }
 
@@ -323,7 +330,7 @@ extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t
                                  size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
-  if ((s = check_kmeans_alignment(x, centroids))) return s;
+  if ((s = check_kmeans_alignment(x, centroids, workspace))) return s;
   if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
     return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);
   Carver c(workspace, workspace_bytes);
@@ -331,8 +338,8 @@ extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t
   if (!c.ok() || !workspace) return fail(SPR_ERR_WORKSPACE, "k-means assign: workspace %zu < %zu", workspace_bytes, c.off);
   cudaStream_t st = (cudaStream_t)stream;
   cudaMemsetAsync(w.err, 0, sizeof(int), st);
-  if ((s = launch_point_sq(x, x_dtype, bh, n, d, w.xsq, st))) return s;
-  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.csq, precision, labels, nullptr, w.err, st);
+  if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st))) return s;
+  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, precision, labels, nullptr, w.err, st);
 }
 
 extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
@@ -352,7 +359,7 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
                                 void* workspace, size_t workspace_bytes, void* stream) {
   int s = validate_kmeans(x_dtype, bh, n, d, k);
   if (s) return s;
-  if ((s = check_kmeans_alignment(x, centroids))) return s;
+  if ((s = check_kmeans_alignment(x, centroids, workspace))) return s;
   if (iters < 1 || iters > 1024) return fail(SPR_ERR_ARG, "k-means: iters=%d must be in [1,1024]", iters);
   if (precision != SPR_KMEANS_TF32 && precision != SPR_KMEANS_FP32)
     return fail(SPR_ERR_ARG, "k-means: unknown precision %d", precision);
@@ -368,9 +375,9 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
   cudaMemsetAsync(w.err, 0, (size_t)((char*)(w.shifts + 1024) - (char*)w.err), st);
   cudaMemsetAsync(iters_done, 0, sizeof(int32_t), st);
   const int64_t count = bh * k * (int64_t)d;
-  if ((s = launch_point_sq(x, x_dtype, bh, n, d, w.xsq, st))) return s;
+  if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st))) return s;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.csq, precision, labels, done, w.err, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, precision, labels, done, w.err, st))) return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))

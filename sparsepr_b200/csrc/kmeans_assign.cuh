@@ -17,6 +17,7 @@
 // holds two 128-column accumulators so the argmin of one tile overlaps the
 // next GEMM, across item boundaries too.
 #pragma once
+#include <cuda.h>
 #include "tc_common.cuh"
 
 namespace spr {
@@ -400,18 +401,499 @@ static int launch_assign_dp(const void* x, int64_t bh, int64_t n, int d, int k, 
   }
 }
 
-// |x|^2 for fp32 points (call once per k-means run: x does not change).
-inline int launch_point_sq(const void* x, int x_dtype, int64_t bh, int64_t n, int d, float* xsq, cudaStream_t st) {
+// ---------------------------------------------------------------------------
+// TMA variant for fp32 points at TF32 precision (the routing path).
+//
+// One thread streams tiles with tiled TMA loads (128-byte swizzle, zero fill
+// past the last point / centroid / feature), so the loads cost a handful of
+// instructions per tile instead of one cp.async per 16 bytes.  For d <= 64 an
+// item is 256 points (two 128-row M tiles): each centroid tile feeds two MMAs,
+// halving centroid traffic and the per-tile barrier round trips; TMEM holds
+// 2 buffers x 2 M tiles x 128 columns (all 512 columns).
+//
+// Argmin as one integer minimum per column.  Per problem b the host-side
+// prologue (point_sqmax_kernel, centroid_bias_kernel) provides a bias
+// B >= max|x|^2 and the biased norms |c|^2 + B, so that per column
+//     s = (|c|^2 + B) - 2 x.c = dist + (B - |x|^2)
+// is one FFMA, strictly positive and within 2^12 of base = B / 256.  For
+// positive floats the bit pattern orders like the value, so
+//     key = 32 * (bits(s) - bits(base)) + j      (j = column within 32)
+// is exact (fp32 order, ties to the lower column) and fits 32 bits: one IMAD
+// and one unsigned min per column.  Columns with dist <= 0 (s <= B - |x|^2)
+// are clamped to distance 0 as the reference does, lowest index first, on a
+// warp-uniform slow path that only runs when such a column exists.
+//
+// |x|^2 is computed by the argmin threads from the staged point tile.
+//
+// Warps 0-7: argmin (thread = point when MT == 2; two threads per point, one
+// per 64-column half, when MT == 1), warp 8: MMA issuer, warp 9: TMA producer.
+constexpr int kTmaAsgThreads = 320;
+
+template <int DP>
+struct TmaAsg {
+  static constexpr int kMT = DP <= 64 ? 2 : 1;   // 128-point M tiles per item
+  static constexpr int kBlocks = DP / 32;         // 128-byte column blocks per row
+  static constexpr int kTileBytes = 128 * DP * 4; // one 128-row tile of points or centroids
+  static constexpr int kXBytes = kMT * kTileBytes;
+  static constexpr int kBudget = 216 * 1024;
+  static constexpr int kNX = (1024 + 2 * kXBytes + 2 * kTileBytes <= kBudget) ? 2 : 1;
+  static constexpr int kNC = (1024 + kNX * kXBytes + 4 * kTileBytes <= kBudget)   ? 4
+                             : (1024 + kNX * kXBytes + 3 * kTileBytes <= kBudget) ? 3
+                                                                                  : 2;
+  static constexpr int kTotal = 1024 + kNX * kXBytes + kNC * kTileBytes;
+  static constexpr int kCG = 2 / kMT;  // argmin threads per point
+  static constexpr int kNQ = 8;        // |c|^2 ring slots
+};
+
+// max over the points of problem b of |x|^2 into xmax[b] (zeroed by the caller).
+__global__ void point_sqmax_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ xmax) {
+  __shared__ float s_max[8];
+  const int64_t b = blockIdx.y;
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float s = 0.f;
+  if (p < n) {
+    const float4* r = reinterpret_cast<const float4*>(x + (b * n + p) * d);
+    for (int e = 0; e < d / 4; ++e) {
+      const float4 v = r[e];
+      s = fmaf(v.x, v.x, s);
+      s = fmaf(v.y, v.y, s);
+      s = fmaf(v.z, v.z, s);
+      s = fmaf(v.w, v.w, s);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) s = fmaxf(s, s_max[w]);
+    atomicMax(reinterpret_cast<int*>(xmax + b), __float_as_int(s));  // non-negative floats order as ints
+  }
+}
+
+// Per problem b: csqb[b][j] = |c_j|^2 + B for j < k (0 in the padding up to
+// kpad = 128 * centroid tiles) and bias[b] = (B, base) with
+//   B = max|x|^2 * (1 + 2^-7) + max|c|^2 / 4,   base = B / 256.
+// Then s = |c|^2 + B - 2 x.c lies in (2^-7 B - e, 10 B] for every point of b
+// (e = TF32 error of 2 x.c, at most 2^-9 B), i.e. above base and below
+// 2^12 base.
+//
+// Grid (centroid blocks of 128, bh); thread = centroid.  Each block folds its
+// maximum into cmax[b]; the last block of a problem (ticket counter) adds B to
+// the whole row and resets cmax[b] and the counter to 0 for the next call.
+// cmax and count must be zero before the first call.
+__global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restrict__ c, int k, int d, int kpad,
+                                                            const float* __restrict__ xmax, float* __restrict__ csqb,
+                                                            float* __restrict__ bias, float* __restrict__ cmax,
+                                                            unsigned* __restrict__ count, const int* __restrict__ done) {
+  if (done && *done) return;
+  __shared__ float s_max[4];
+  __shared__ bool s_last;
+  const int64_t b = blockIdx.y;
+  const int i = blockIdx.x * 128 + threadIdx.x;
+  float* out = csqb + b * kpad;
+  float s = 0.f;
+  if (i < k) {
+    const float4* r = reinterpret_cast<const float4*>(c + (b * k + i) * d);
+    for (int e = 0; e < d / 4; ++e) {
+      const float4 v = r[e];
+      s = fmaf(v.x, v.x, s);
+      s = fmaf(v.y, v.y, s);
+      s = fmaf(v.z, v.z, s);
+      s = fmaf(v.w, v.w, s);
+    }
+    out[i] = s;
+  }
+  float m = s;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    m = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
+    atomicMax(reinterpret_cast<int*>(cmax + b), __float_as_int(m));
+    __threadfence();
+    s_last = atomicAdd(count + b, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float cm = __int_as_float(atomicAdd(reinterpret_cast<int*>(cmax + b), 0));
+  const float B = fmaf(__ldcg(xmax + b), 1.0078125f, 0.25f * cm) + 1e-30f;
+  for (int j = threadIdx.x; j < kpad; j += blockDim.x) out[j] = j < k ? __ldcg(out + j) + B : 0.f;
+  if (threadIdx.x == 0) {
+    bias[2 * b] = B;
+    bias[2 * b + 1] = B * 0.00390625f;
+    cmax[b] = 0.f;
+    count[b] = 0u;
+  }
+}
+
+template <int DP>
+__global__ void __launch_bounds__(kTmaAsgThreads, 1)
+assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap, int64_t n,
+                  int d, int k, int64_t items, const float* __restrict__ csqb, const float* __restrict__ bias,
+                  int32_t* __restrict__ labels, const int* __restrict__ done, int* __restrict__ err) {
+  using L = TmaAsg<DP>;
+  constexpr int MT = L::kMT, NX = L::kNX, NC = L::kNC, NQ = L::kNQ, CG = L::kCG;
+  constexpr int kBlocksPerThread = 4 / CG;  // 32-column TMEM blocks scanned per tile
+  if (done && *done) return;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_x_full[NX], bar_x_empty[NX], bar_x_read[NX];
+  __shared__ uint64_t bar_c_full[NC], bar_c_empty[NC], bar_q_full[NQ], bar_q_read[NQ];
+  __shared__ uint64_t bar_d_full[2], bar_d_free[2], bar_mma_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ __align__(128) float s_csq[NQ][kAsgN];
+  __shared__ float s_best[kAsgM];
+  __shared__ int s_best_idx[kAsgM];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sx0 = tc::smem_addr(smem);
+  const uint32_t sc0 = sx0 + NX * L::kXBytes;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ctiles = (k + kAsgN - 1) / kAsgN;
+  const int64_t ptiles = (n + MT * kAsgM - 1) / (MT * kAsgM);
+
+  if (tid == 0) {
+    for (int i = 0; i < NX; ++i) {
+      tc::mbar_init(&bar_x_full[i], 1);
+      tc::mbar_init(&bar_x_empty[i], 1);
+      tc::mbar_init(&bar_x_read[i], kAsgEpilogue);
+    }
+    for (int i = 0; i < NC; ++i) {
+      tc::mbar_init(&bar_c_full[i], 1);
+      tc::mbar_init(&bar_c_empty[i], 1);
+    }
+    for (int i = 0; i < NQ; ++i) {
+      tc::mbar_init(&bar_q_full[i], 1);
+      tc::mbar_init(&bar_q_read[i], kAsgEpilogue);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&bar_d_full[i], 1);
+      tc::mbar_init(&bar_d_free[i], kAsgEpilogue);
+    }
+    tc::mbar_init(&bar_mma_done, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == 9 && lane == 0) {
+    tc::prefetch_tmap(&xmap);
+    tc::prefetch_tmap(&cmap);
+  }
+  if (warp == 8) tc::tmem_alloc<256 * MT>(&s_tmem);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 9) {
+    // ---------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int64_t nc = 0;  // centroid tiles issued
+      int nx = 0;      // point items issued
+      bool ok = true;
+      for (int64_t it = blockIdx.x; ok && it < items; it += gridDim.x) {
+        const int b = (int)(it / ptiles);
+        const int64_t p0 = (it % ptiles) * (MT * kAsgM);
+        const int xb = nx % NX;
+        if (nx >= NX) {  // the GEMMs and the |x|^2 reads of item nx-NX are done with this buffer
+          const uint32_t par = ((nx / NX) - 1) & 1;
+          if (!(ok = tc::mbar_wait(&bar_x_empty[xb], par, err, 31) && tc::mbar_wait(&bar_x_read[xb], par, err, 31)))
+            break;
+        }
+        const uint32_t xbase = sx0 + xb * L::kXBytes;
+        const int mts = p0 + kAsgM < n ? MT : 1;  // an M tile wholly past the last point is not loaded
+        tc::mbar_expect_tx(&bar_x_full[xb], (uint32_t)(mts * L::kTileBytes));
+        for (int mt = 0; mt < mts; ++mt)
+#pragma unroll
+          for (int j = 0; j < L::kBlocks; ++j)
+            tc::tma_load_3d(xbase + mt * L::kTileBytes + j * (kAsgM * 128), &xmap, 32 * j, (int)(p0 + mt * kAsgM), b,
+                            &bar_x_full[xb]);
+        ++nx;
+        for (int t = 0; t < ctiles; ++t) {
+          const int st = (int)(nc % NC), q = (int)(nc % NQ);
+          if (nc >= NC && !(ok = tc::mbar_wait(&bar_c_empty[st], (uint32_t)(((nc / NC) - 1) & 1), err, 32))) break;
+          if (nc >= NQ && !(ok = tc::mbar_wait(&bar_q_read[q], (uint32_t)(((nc / NQ) - 1) & 1), err, 32))) break;
+          const uint32_t cbase = sc0 + st * L::kTileBytes;
+          tc::mbar_expect_tx(&bar_c_full[st], (uint32_t)L::kTileBytes);
+#pragma unroll
+          for (int j = 0; j < L::kBlocks; ++j)
+            tc::tma_load_3d(cbase + j * (kAsgN * 128), &cmap, 32 * j, t * kAsgN, b, &bar_c_full[st]);
+          tc::mbar_expect_tx(&bar_q_full[q], kAsgN * 4);
+          tc::bulk_load(tc::smem_addr(&s_csq[q][0]), csqb + ((int64_t)b * ctiles + t) * kAsgN, kAsgN * 4,
+                        &bar_q_full[q]);
+          ++nc;
+        }
+      }
+      // Let every copy issued here land before the CTA exits (matters only
+      // when a wait gave up and the consumers stopped early).
+      for (int u = nx > NX ? nx - NX : 0; u < nx; ++u) tc::mbar_drain(&bar_x_full[u % NX], (u / NX) & 1);
+      for (int64_t u = nc > NC ? nc - NC : 0; u < nc; ++u)
+        tc::mbar_drain(&bar_c_full[u % NC], (uint32_t)((u / NC) & 1));
+      for (int64_t u = nc > NQ ? nc - NQ : 0; u < nc; ++u)
+        tc::mbar_drain(&bar_q_full[u % NQ], (uint32_t)((u / NQ) & 1));
+    }
+  } else if (warp == 8) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const int ksteps = (d + 7) / 8;
+      int64_t gt = 0;
+      int il = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; ok && it < items; it += gridDim.x, ++il) {
+        const int xb = il % NX;
+        if (!(ok = tc::mbar_wait(&bar_x_full[xb], (il / NX) & 1, err, 33))) break;
+        const uint32_t xbase = sx0 + xb * L::kXBytes;
+        for (int t = 0; t < ctiles; ++t, ++gt) {
+          const int st = (int)(gt % NC);
+          const int db = (int)(gt & 1);
+          if (!(ok = tc::mbar_wait(&bar_c_full[st], (uint32_t)((gt / NC) & 1), err, 33))) break;
+          if (gt >= 2 && !(ok = tc::mbar_wait(&bar_d_free[db], (uint32_t)(((gt >> 1) - 1) & 1), err, 33))) break;
+          tc::tc_fence_after();
+          const uint32_t cbase = sc0 + st * L::kTileBytes;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t dt = tmem + (uint32_t)(db * MT + mt) * 128;
+            // 8 tf32 (32 bytes) per MMA K step; steps wholly inside the zero
+            // padding past d are skipped.
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t kb = kk * 32;
+              const uint32_t off = (kb >> 7) * (kAsgM * 128) + (kb & 127);
+              tc::mma_tf32(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
+                           tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, kk > 0);
+            }
+          }
+          tc::mma_commit(&bar_d_full[db]);
+          tc::mma_commit(&bar_c_empty[st]);
+          if (t == ctiles - 1) tc::mma_commit(&bar_x_empty[xb]);
+        }
+      }
+      tc::mma_commit(&bar_mma_done);  // every MMA issued above has finished before TMEM is freed
+      tc::mbar_drain(&bar_mma_done, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- argmin epilogue
+    const int row = tid & 127;  // TMEM lane = point row within its M tile
+    const int sub = tid >> 7;
+    const int mt = MT == 2 ? sub : 0;
+    const int cg = MT == 2 ? 0 : sub;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    int64_t gt = 0;
+    int il = 0;
+    bool ok = true;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++il) {
+      const int64_t b = it / ptiles;
+      const int64_t p = (it % ptiles) * (MT * kAsgM) + mt * kAsgM + row;
+      const int xb = il % NX;
+      ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_x_full[xb], (il / NX) & 1, err, 34));
+      // |x|^2 of this point from the staged tile (zero padding adds nothing).
+      float xsq = 0.f;
+      if (ok) {
+        const uint8_t* xt = smem + xb * L::kXBytes + mt * L::kTileBytes;
+#pragma unroll
+        for (int ch = 0; ch < DP / 4; ++ch) {
+          const float4 v = *reinterpret_cast<const float4*>(xt + tc::sw128_off(row, ch, kAsgM));
+          xsq = fmaf(v.x, v.x, xsq);
+          xsq = fmaf(v.y, v.y, xsq);
+          xsq = fmaf(v.z, v.z, xsq);
+          xsq = fmaf(v.w, v.w, xsq);
+        }
+      }
+      tc::mbar_arrive(&bar_x_read[xb]);
+      const float B = __ldg(bias + 2 * b), base = __ldg(bias + 2 * b + 1);
+      // key = 32 * (bits(s) - bits(base)) + j, computed mod 2^32 as bits(s) * 32 + kj[j].
+      const uint32_t koff = 0u - 32u * __float_as_uint(base);
+      uint32_t kj[32];  // per-column key offsets, kept in registers for the item
+#pragma unroll
+      for (int j = 0; j < 32; ++j) kj[j] = koff + j;
+      // Columns with s <= thr have dist <= 0 (clamped to 0 by the reference).
+      const uint32_t thrq = __float_as_uint(B - xsq) - __float_as_uint(base);
+      uint32_t best_q = 0xffffffffu;  // bits(s) - bits(base) of the best column so far
+      int best_idx = 0;
+      for (int t = 0; t < ctiles; ++t, ++gt) {
+        const int db = (int)(gt & 1);
+        const int q = (int)(gt % NQ);
+        ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[db], (uint32_t)((gt >> 1) & 1), err, 34));
+        ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_q_full[q], (uint32_t)((gt / NQ) & 1), err, 34));
+        tc::tc_fence_after();
+        const int k0 = t * kAsgN;
+        if (ok) {
+          const bool full = k0 + kAsgN <= k;  // only the last centroid tile is partial
+          const uint32_t tbase = tmem + lane_base + (uint32_t)(db * MT + mt) * 128 + cg * kBlocksPerThread * 32;
+          // Double-buffered TMEM reads: block i+1 is in flight while block i is scanned.
+          float accv[2][32];
+          tc::tmem_ld32_async(tbase, accv[0]);
+          tc::tmem_wait_ld();
+          tc::reg_fence32(accv[0]);
+#pragma unroll
+          for (int i = 0; i < kBlocksPerThread; ++i) {
+            float* acc = accv[i & 1];
+            if (i + 1 < kBlocksPerThread) tc::tmem_ld32_async(tbase + (i + 1) * 32, accv[(i + 1) & 1]);
+            const int cb = cg * kBlocksPerThread + i;
+            const float* cq = &s_csq[q][cb * 32];
+            const int lim = full ? 32 : k - (k0 + cb * 32);  // valid columns in this block (may be <= 0)
+            // Four independent minimum chains (columns j mod 4); keys are
+            // distinct per column, so the merged minimum is the same.
+            uint32_t m0 = 0xffffffffu, m1 = 0xffffffffu, m2 = 0xffffffffu, m3 = 0xffffffffu;
+            if (full) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 c4 = *reinterpret_cast<const float4*>(cq + j);
+                m0 = min(m0, __float_as_uint(fmaf(-2.f, acc[j], c4.x)) * 32u + kj[j]);
+                m1 = min(m1, __float_as_uint(fmaf(-2.f, acc[j + 1], c4.y)) * 32u + kj[j + 1]);
+                m2 = min(m2, __float_as_uint(fmaf(-2.f, acc[j + 2], c4.z)) * 32u + kj[j + 2]);
+                m3 = min(m3, __float_as_uint(fmaf(-2.f, acc[j + 3], c4.w)) * 32u + kj[j + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const uint32_t key = __float_as_uint(fmaf(-2.f, acc[j], cq[j])) * 32u + kj[j];
+                m0 = j < lim ? min(m0, key) : m0;
+              }
+            }
+            const uint32_t kmin = min(min(m0, m1), min(m2, m3));
+            uint32_t qv = kmin >> 5;
+            int jj = (int)(kmin & 31u);
+            if (__any_sync(0xffffffffu, qv <= thrq && lim > 0)) {
+              // Rare: a column at distance <= 0.  All such columns tie at 0;
+              // the lowest one wins.
+              if (qv <= thrq && lim > 0) {
+                int first = 31;
+#pragma unroll
+                for (int j = 31; j >= 0; --j) {
+                  const uint32_t sq = __float_as_uint(fmaf(-2.f, acc[j], cq[j])) - __float_as_uint(base);
+                  if (j < lim && sq <= thrq) first = j;
+                }
+                jj = first;
+                qv = thrq;
+              }
+            }
+            if (lim > 0 && qv < best_q) {  // strict: an earlier column keeps a tie
+              best_q = qv;
+              best_idx = k0 + cb * 32 + jj;
+            }
+            if (i + 1 < kBlocksPerThread) {
+              tc::tmem_wait_ld();
+              tc::reg_fence32(accv[(i + 1) & 1]);
+            }
+          }
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bar_d_free[db]);
+        tc::mbar_arrive(&bar_q_read[q]);
+      }
+      if constexpr (CG == 2) {
+        // Merge the two column halves of each point (equal values: lower index).
+        if (cg == 1) { s_best[row] = __uint_as_float(best_q); s_best_idx[row] = best_idx; }
+        tc::named_bar(1, kAsgEpilogue);
+        if (cg == 0) {
+          const uint32_t ob = __float_as_uint(s_best[row]);
+          const int oi = s_best_idx[row];
+          if (ob < best_q || (ob == best_q && oi < best_idx)) best_idx = oi;
+          if (p < n) labels[b * n + p] = best_idx;
+        }
+        tc::named_bar(1, kAsgEpilogue);
+      } else {
+        if (p < n) labels[b * n + p] = best_idx;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc<256 * MT>(tmem);
+  }
+}
+
+// 3-D map over [bh][rows][d] fp32 rows: box 32 features x 128 rows x 1, 128-byte swizzle.
+inline int encode_row_map(CUtensorMap* m, const float* base, int d, int64_t rows, int64_t bh, const char* what) {
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)d * 4, (cuuint64_t)rows * d * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)kAsgM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  // Resolved through the runtime so the library does not link libcuda itself.
+  using EncodeFn = decltype(&cuTensorMapEncodeTiled);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return fail(SPR_ERR_LAUNCH, "k-means assign: cuTensorMapEncodeTiled is unavailable");
+    encode = reinterpret_cast<EncodeFn>(fn);
+  }
+  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPR_ERR_LAUNCH, "k-means assign: tensor map for %s failed (CUresult %d)", what, (int)r);
+  return SPR_OK;
+}
+
+template <int DP>
+static int launch_assign_tma(const float* x, int64_t bh, int64_t n, int d, int k, const float* c,
+                             const float* csqb, const float* bias, int32_t* labels, const int* done, int* err,
+                             cudaStream_t st) {
+  using L = TmaAsg<DP>;
+  CUtensorMap xmap, cmap;
+  int s = encode_row_map(&xmap, x, d, n, bh, "points");
+  if (!s) s = encode_row_map(&cmap, c, d, k, bh, "centroids");
+  if (s) return s;
+  auto kern = assign_tma_kernel<DP>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t items = bh * ((n + L::kMT * kAsgM - 1) / (L::kMT * kAsgM));
+  const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
+  kern<<<grid, kTmaAsgThreads, L::kTotal, st>>>(xmap, cmap, n, d, k, items, csqb, bias, labels, done, err);
+  return check_launch("k-means assign (tcgen05, TMA)");
+}
+
+// Padded |c|^2 entries needed by the TMA path: [bh][128 * centroid tiles].
+inline size_t centroid_sq_pad_count(int64_t bh, int k) { return (size_t)bh * (size_t)((k + kAsgN - 1) / kAsgN) * kAsgN; }
+
+// The TMA path serves fp32 points at TF32 precision; other cases use the
+// register-staged kernel above.
+inline bool assign_uses_tma(int x_dtype, int precision) { return x_dtype == SPR_F32 && precision == SPR_KMEANS_TF32; }
+
+// Per-run point statistics (call once per k-means run: x does not change):
+// |x|^2 per point for the register path, max |x|^2 per problem for the TMA
+// path (which computes |x|^2 itself).
+inline int launch_point_sq(const void* x, int x_dtype, int precision, int64_t bh, int64_t n, int d, float* xsq,
+                           float* xmax, cudaStream_t st) {
+  if (assign_uses_tma(x_dtype, precision)) {
+    // xmax and the bias scratch that follows it (4 * bh words) start at 0.
+    cudaMemsetAsync(xmax, 0, (size_t)bh * 5 * sizeof(float), st);
+    point_sqmax_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)bh), 256, 0, st>>>((const float*)x, n, d, xmax);
+    return check_launch("point norm maxima");
+  }
   if (x_dtype != SPR_F32) return SPR_OK;  // other dtypes compute |x|^2 inside the assignment kernel
   const int64_t rows = bh * n;
   row_sq_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>((const float*)x, rows, d, xsq, nullptr);
   return check_launch("point norms");
 }
 
-// |c|^2 of the current centroids, then the assignment GEMM (xsq from launch_point_sq).
+// Centroid norms of the current centroids, then the assignment GEMM (point
+// statistics from launch_point_sq).  csq holds centroid_sq_pad_count floats,
+// bias 4 * bh: (B, base) pairs, then the centroid-norm maxima and counters of
+// centroid_bias_kernel (zeroed once per run by launch_point_sq).
 inline int launch_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, const float* c,
-                         const float* xsq, float* csq, int precision, int32_t* labels, const int* done, int* err,
-                         cudaStream_t st) {
+                         const float* xsq, const float* xmax, float* csq, float* bias, int precision, int32_t* labels,
+                         const int* done, int* err, cudaStream_t st) {
+  if (assign_uses_tma(x_dtype, precision)) {
+    const int kpad = (k + kAsgN - 1) / kAsgN * kAsgN;
+    centroid_bias_kernel<<<dim3((unsigned)(kpad / kAsgN), (unsigned)bh), 128, 0, st>>>(c, k, d, kpad, xmax, csq, bias,
+                                                                                     bias + 2 * bh,
+                                                                                     reinterpret_cast<unsigned*>(bias + 3 * bh),
+                                                                                     done);
+    int s = check_launch("centroid norms");
+    if (s) return s;
+    const float* xf = (const float*)x;
+    if (d <= 32) return launch_assign_tma<32>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
+    if (d <= 64) return launch_assign_tma<64>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
+    if (d <= 96) return launch_assign_tma<96>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
+    return launch_assign_tma<128>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
+  }
   const int64_t crows = bh * k;
   row_sq_kernel<<<(unsigned)((crows * 32 + 255) / 256), 256, 0, st>>>(c, crows, d, csq, done);
   int s = check_launch("centroid norms");

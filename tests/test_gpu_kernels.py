@@ -37,10 +37,29 @@ def test_assign_matches_oracle(cuda, d, dtype, precision, rel):
     assert (got == ref).float().mean() > 0.98
 
 
-def test_assign_ties_go_to_lowest_index(cuda):
-    x = torch.zeros(1, 64, 16)
-    c = torch.zeros(1, 200, 16)  # every centroid equidistant
-    assert K.kmeans_assign(x.to(cuda), c.to(cuda), "fp32").max().item() == 0
+@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+@pytest.mark.parametrize("d", [16, 48, 64])
+def test_assign_ties_go_to_lowest_index(cuda, precision, d):
+    x = torch.zeros(2, 300, d)
+    c = torch.zeros(2, 200, d)  # every centroid at distance 0
+    assert K.kmeans_assign(x.to(cuda), c.to(cuda), precision).max().item() == 0
+
+
+@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+def test_assign_coincident_points_clamp_to_zero(cuda, precision):
+    """Points equal to a centroid that appears several times: the distance is
+    0 up to rounding (clamped at 0 by the reference), so the lowest copy wins."""
+    g = torch.Generator().manual_seed(5)
+    c = torch.randn(2, 300, 48, generator=g) * 3
+    c[:, 150] = c[:, 40]
+    c[:, 250] = c[:, 40]
+    x = torch.randn(2, 700, 48, generator=g) * 3
+    x[:, :100] = c[:, 40:41]
+    x[:, 100:200] = c[:, 5:6]
+    got = K.kmeans_assign(x.to(cuda), c.to(cuda), precision).cpu()
+    assert (got[:, :100] == 40).all()
+    assert (got[:, 100:200] == 5).all()
+    assert torch.equal(got.long(), oracle.euclid_assign(x, c)) or (got.long() == oracle.euclid_assign(x, c)).float().mean() > 0.99
 
 
 @pytest.mark.parametrize("n,k", [(1, 1), (5000, 7), (70001, 1000), (4097, 3000)])
