@@ -106,6 +106,24 @@ def _dist():
     return world, rank, local
 
 
+def _print_kernel_table(step, q, k, v, dev):
+    """Per-kernel device time of one layer (torch profiler, CUDA activity) to stdout.
+
+    A profiling aid: the numbers include profiler overhead and are not bench values."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step(q, k, v)
+        torch.cuda.synchronize(dev)
+    rows = [(e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0]
+    total = sum(r[0] for r in rows)
+    print(f"{'kernel':72s} {'calls':>6s} {'ms':>9s} {'share':>7s}")
+    for t, n, name in sorted(rows, reverse=True):
+        print(f"{name[:72]:72s} {n:6d} {t / 1e3:9.3f} {100 * t / total:6.1f}%")
+    print(f"{'total':72s} {'':6s} {total / 1e3:9.3f}")
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -145,6 +163,10 @@ def run_b200(args):
     sel_keys = (route.video_dynamic_map.long() * route.k_cluster_sizes.long().unsqueeze(1)).sum(-1)
     attn_flops = int((4 * 128 * (sel_keys * route.q_cluster_sizes.long()).sum()).item())
     del out, info, route
+
+    if args.kernel_table:
+        _print_kernel_table(step, q, k, v, dev)
+        return
 
     # Eager pass: per-kernel events for the attention roofline and the launch count.
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -301,6 +323,8 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
+    ap.add_argument("--kernel-table", action="store_true",
+                    help="print per-kernel device times of one layer (torch profiler) instead of the bench line")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -121,11 +121,18 @@ int spr_permute_rows(const void* x, const int32_t* idx, void* y, int64_t bh, int
 /*
  * Attention-mass selector scores: scores[b,q,c] = log sum_{t in cluster c}
  * exp(qc[b,q].k_sorted[b,t] / sqrt(d)), -inf for empty clusters.
- * q_centroids [bh,cq,d] fp32, k_sorted [bh,n,d] bf16, k_offsets [bh,ck+1] i32.
+ * q_centroids [bh,cq,d] fp32, k_sorted [bh,n,d] bf16, k_offsets [bh,ck+1] i32;
+ * d = 128.  Tensor cores: each centroid as three bf16 parts, fp32 accumulation.
  * Replaces kernels/triton/svg_ear.py:372-450 attention_mass_scores_triton (kernel 7-92).
  */
 int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets,
                               int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream);
+
+/*
+ * Status of the last spr_attention_mass_scores launch (synchronous copy):
+ * *out = 0, or the code of a device-side bounded wait that gave up.
+ */
+int spr_attention_mass_scores_status(int* out);
 
 /*
  * Budgeted cluster selection per (b, q): descending score (ties -> lower

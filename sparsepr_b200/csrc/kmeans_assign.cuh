@@ -17,8 +17,8 @@
 // holds two 128-column accumulators so the argmin of one tile overlaps the
 // next GEMM, across item boundaries too.
 #pragma once
-#include <cuda.h>
 #include "tc_common.cuh"
+#include "tmap.cuh"
 
 namespace spr {
 
@@ -806,27 +806,7 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
 
 // 3-D map over [bh][rows][d] fp32 rows: box 32 features x 128 rows x 1, 128-byte swizzle.
 inline int encode_row_map(CUtensorMap* m, const float* base, int d, int64_t rows, int64_t bh, const char* what) {
-  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)bh};
-  cuuint64_t strides[2] = {(cuuint64_t)d * 4, (cuuint64_t)rows * d * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)kAsgM, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  // Resolved through the runtime so the library does not link libcuda itself.
-  using EncodeFn = decltype(&cuTensorMapEncodeTiled);
-  static EncodeFn encode = nullptr;
-  if (!encode) {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      return fail(SPR_ERR_LAUNCH, "k-means assign: cuTensorMapEncodeTiled is unavailable");
-    encode = reinterpret_cast<EncodeFn>(fn);
-  }
-  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
-                                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(SPR_ERR_LAUNCH, "k-means assign: tensor map for %s failed (CUresult %d)", what, (int)r);
-  return SPR_OK;
+  return encode_map_3d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, d, rows, bh, 32, kAsgM, what);
 }
 
 template <int DP>

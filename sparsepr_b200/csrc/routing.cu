@@ -1,86 +1,9 @@
-// Routing kernels: attention-mass selector scores and the budgeted
-// cluster selector (sort + prefix budget + crossing cluster + compaction).
+// Routing kernel: the budgeted cluster selector (sort + prefix budget +
+// crossing cluster + compaction).  The attention-mass scores are in scores.cu.
 #include "common.cuh"
 
 namespace spr {
 
-constexpr int kScoreTok = 16;  // key rows staged per step
-
-// One block per (key cluster, problem); each thread owns query centroids and
-// keeps an online log-sum-exp over the cluster's key rows (exact fp32 dots).
-__global__ void __launch_bounds__(256)
-attention_mass_scores_kernel(const float* __restrict__ qc, const __nv_bfloat16* __restrict__ ks,
-                             const int32_t* __restrict__ koff, int cq, int ck, int64_t n,
-                             float* __restrict__ scores) {
-  constexpr int D = 128;
-  __shared__ __align__(16) float sh_k[kScoreTok][D];
-  const int c = blockIdx.x;
-  const int64_t b = blockIdx.y;
-  const int32_t beg = koff[b * (ck + 1) + c], end = koff[b * (ck + 1) + c + 1];
-  const float scale = rsqrtf((float)D);
-  const float* qb = qc + b * (int64_t)cq * D;
-  const __nv_bfloat16* kb = ks + b * n * D;
-  // Up to 2 query centroids per thread (cq <= 512).
-  float m[2] = {-INFINITY, -INFINITY}, s[2] = {0.f, 0.f};
-  for (int32_t t0 = beg; t0 < end; t0 += kScoreTok) {
-    const int nt = min(kScoreTok, end - t0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < kScoreTok * D / 8; i += blockDim.x) {
-      const int r = i / (D / 8), cidx = i % (D / 8);
-      float f[8];
-      if (r < nt) {
-        const uint4 v = reinterpret_cast<const uint4*>(kb + (int64_t)(t0 + r) * D)[cidx];
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(h[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sh_k[r][cidx * 8 + e] = f[e];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-      const int q = threadIdx.x + slot * blockDim.x;
-      if (q >= cq) continue;
-      const float4* q4 = reinterpret_cast<const float4*>(qb + (int64_t)q * D);
-      float dots[kScoreTok];
-#pragma unroll
-      for (int j = 0; j < kScoreTok; ++j) dots[j] = 0.f;
-      for (int e4 = 0; e4 < D / 4; ++e4) {
-        const float4 qv = __ldg(q4 + e4);
-#pragma unroll
-        for (int j = 0; j < kScoreTok; ++j) {
-          const float4 kv = reinterpret_cast<const float4*>(sh_k[j])[e4];
-          dots[j] = fmaf(qv.x, kv.x, dots[j]);
-          dots[j] = fmaf(qv.y, kv.y, dots[j]);
-          dots[j] = fmaf(qv.z, kv.z, dots[j]);
-          dots[j] = fmaf(qv.w, kv.w, dots[j]);
-        }
-      }
-      float cm = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < kScoreTok; ++j)
-        if (j < nt) cm = fmaxf(cm, dots[j] * scale);
-      const float nm = fmaxf(m[slot], cm);
-      float acc = s[slot] * __expf(m[slot] - nm);
-#pragma unroll
-      for (int j = 0; j < kScoreTok; ++j)
-        if (j < nt) acc += __expf(dots[j] * scale - nm);
-      s[slot] = acc;
-      m[slot] = nm;
-    }
-  }
-#pragma unroll
-  for (int slot = 0; slot < 2; ++slot) {
-    const int q = threadIdx.x + slot * blockDim.x;
-    if (q >= cq) continue;
-    const float v = end > beg ? logf(fmaxf(s[slot], 1e-30f)) + m[slot] : -INFINITY;
-    scores[(b * cq + q) * (int64_t)ck + c] = v;
-  }
-}
 
 __device__ __forceinline__ uint32_t float_order_desc(float f) {
   uint32_t u = __float_as_uint(f);
@@ -191,19 +114,6 @@ select_budget_kernel(const float* __restrict__ scores, const int32_t* __restrict
 }  // namespace spr
 
 using namespace spr;
-
-extern "C" int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets,
-                                         int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream) {
-  if (d != 128) return fail(SPR_ERR_SHAPE, "attention-mass scores require d=128, got %d", d);
-  if (bh <= 0 || cq <= 0 || ck <= 0 || cq > 512 || bh > 65535)
-    return fail(SPR_ERR_SHAPE, "attention-mass scores: bad shape bh=%lld cq=%d ck=%d", (long long)bh, cq, ck);
-  if (!aligned(q_centroids, 16) || !aligned(k_sorted, 16))
-    return fail(SPR_ERR_ALIGN, "attention-mass scores: 16-byte alignment required");
-  dim3 grid((unsigned)ck, (unsigned)bh);
-  attention_mass_scores_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      q_centroids, (const __nv_bfloat16*)k_sorted, k_offsets, cq, ck, n, scores);
-  return check_launch("attention-mass scores");
-}
 
 extern "C" int spr_select_budget(const float* scores, const int32_t* k_sizes, const int32_t* budgets, int64_t bh,
                                  int cq, int ck, uint8_t* routed, int32_t* sel_ids, int32_t* sel_counts, void* stream) {

@@ -178,6 +178,15 @@ def attention_mass_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, k_o
     return scores
 
 
+def scores_error_code() -> int:
+    """Status word of the last attention-mass scores launch (0 = ok; synchronises)."""
+    import ctypes
+
+    v = ctypes.c_int(0)
+    _lib.call("spr_attention_mass_scores_status", ctypes.addressof(v))
+    return v.value
+
+
 def select_budget(scores: torch.Tensor, k_sizes: torch.Tensor, budgets: torch.Tensor):
     """Budgeted selection -> (routed bool [B,Cq+1,Ck+1], sel_ids i32 [B,Cq,Ck], sel_counts i32 [B,Cq])."""
     dev = _cuda(scores, k_sizes, budgets)

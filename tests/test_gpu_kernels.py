@@ -127,16 +127,22 @@ def test_kmeans_bf16_rounded_centroids(cuda):
     assert torch.equal(c.cpu().to(torch.bfloat16).float(), c.cpu())
 
 
-def test_attention_mass_scores(cuda):
-    g = torch.Generator().manual_seed(11)
-    bh, n, cq, ck = 2, 1200, 40, 33
+@pytest.mark.parametrize("bh,n,cq,ck,used,qscale", [
+    (2, 1200, 40, 33, 30, 1.0),      # a few empty clusters at the end
+    (3, 5000, 200, 250, 250, 3.0),   # two centroid tiles, chunk and tile boundaries inside clusters
+    (1, 3000, 20, 5, 5, 1.0),        # clusters much longer than a 128-token tile
+    (2, 700, 129, 64, 20, 2.0),      # most clusters empty; one row in the second centroid tile
+])
+def test_attention_mass_scores(cuda, bh, n, cq, ck, used, qscale):
+    g = torch.Generator().manual_seed(11 + n)
     k = torch.randn(bh, n, 128, generator=g).to(torch.bfloat16)
-    lab = torch.randint(0, ck - 3, (bh, n), generator=g)
+    lab = torch.randint(0, used, (bh, n), generator=g)
     sizes = torch.zeros(bh, ck, dtype=torch.long).scatter_add_(1, lab, torch.ones_like(lab))
-    qc = torch.randn(bh, cq, 128, generator=g)
+    qc = torch.randn(bh, cq, 128, generator=g) * qscale
     ref = oracle.attention_mass_scores(qc, k, sizes)
     off = oracle.cluster_offsets(sizes).to(torch.int32).to(cuda)
     got = K.attention_mass_scores(qc.to(cuda), k.to(cuda), off).cpu()
+    assert K.scores_error_code() == 0
     fin = torch.isfinite(ref)
     assert torch.equal(fin, torch.isfinite(got))
     torch.testing.assert_close(got[fin], ref[fin], atol=2e-4, rtol=1e-5)
