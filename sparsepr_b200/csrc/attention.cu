@@ -9,12 +9,13 @@
 // Warp roles (256 threads):
 //   warps 0-3  softmax: thread t owns query row t (= TMEM lane t).  Loads the
 //              S row from TMEM, online softmax in base 2 with a lazily
-//              updated running max, writes P (bf16) to shared memory, rescales
+//              updated running max, writes P (bf16) to tensor memory, rescales
 //              the O accumulator in TMEM when the max moves, and finally
 //              normalises O and stores the row (through q_order: the inverse
 //              permute is fused into the store).
 //   warp 4     MMA issuer (one thread): S(j) = Q K_j^T into one of two TMEM S
-//              buffers, O += P(j) V_j into the TMEM O accumulator.
+//              buffers, O += P(j) V_j into the TMEM O accumulator with P read
+//              from tensor memory (no shared-memory round trip for P).
 //   warps 5-8  loaders: warps 5-6 gather K rows, warps 7-8 V rows, each into
 //              its own 2-stage ring with 16-byte cp.async.  K stage j is freed
 //              as soon as S(j) is done and V stage j when PV(j) is done, so
@@ -23,7 +24,8 @@
 //              are staged in shared memory once per CTA; each loader lane
 //              resolves one key slot by binary search, and each warp
 //              instruction moves two full 256-byte rows.
-// TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O.
+// TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O,
+// [384,448) is P (bf16 pairs, one 32-bit column per two keys).
 // Operand tiles use the canonical 128-byte-swizzled K-major layout; V is the
 // MN-major B operand of the PV product.
 #include "tc_common.cuh"
@@ -40,7 +42,7 @@ constexpr int kLoaderThreads = 128;
 constexpr int kThreadsTc = 288;
 constexpr int kMaxRuns = 2048;  // key clusters per problem (ck) this kernel accepts
 constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
-constexpr int kSmemTc = 1024 /*align slack*/ + kTileBytes /*Q*/ + 4 * kTileBytes /*K,V x2*/ + kTileBytes /*P*/;
+constexpr int kSmemTc = 1024 /*align slack*/ + kTileBytes /*Q*/ + 4 * kTileBytes /*K,V x2*/;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 1);
 
@@ -96,7 +98,6 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + kTileBytes;        // 2 stages
   uint8_t* sV = sK + 2 * kTileBytes;    // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* qb = q + b * nq * kD;
@@ -208,8 +209,8 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && ntiles > 0) {
       const uint32_t tS[2] = {tmem, tmem + 128};
-      const uint32_t tO = tmem + 256;
-      const uint32_t aq = smem_addr(sQ), ap = smem_addr(sP);
+      const uint32_t tO = tmem + 256, tP = tmem + 384;
+      const uint32_t aq = smem_addr(sQ);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
         if (!mbar_wait(&bar_k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) return false;
@@ -234,10 +235,9 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
         const uint32_t bv = smem_addr(sV + st * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {  // 16 keys per step
-          const uint32_t poff = (kk >> 2) * (kTileM * 128) + (kk & 3) * 32;  // P is K-major over keys
-          const uint32_t voff = kk * 2048;                                   // V is MN-major: 16 rows = 2 x 1024 B
-          mma_f16(tO, sw128_desc(ap + poff, 16, 1024), sw128_desc(bv + voff, kTileN * 128, 1024), kIdescPV,
-                  (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t voff = kk * 2048;  // V is MN-major: 16 rows = 2 x 1024 B
+          mma_f16_ts(tO, tP + kk * 8, sw128_desc(bv + voff, kTileN * 128, 1024), kIdescPV,  // 16 keys = 8 columns
+                     (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&bar_o_done);
         mma_commit(&bar_v_empty[st]);
@@ -308,15 +308,10 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           tmem_wait_st();
         }
       }
-      const uint32_t pbase = smem_addr(sP);
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const uint32_t a = pbase + sw128_off(row, ch, kTileM);
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(pk[ch * 4]), "r"(pk[ch * 4 + 1]),
-                     "r"(pk[ch * 4 + 2]), "r"(pk[ch * 4 + 3])
-                     : "memory");
-      }
-      fence_proxy_async_smem();
+      // P(j) replaces P(j-1), which PV(j-1) (complete, waited above) has read.
+      tmem_st32(tmem + lane_base + 384, reinterpret_cast<const float*>(pk));
+      tmem_st32(tmem + lane_base + 384 + 32, reinterpret_cast<const float*>(pk + 32));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full);
     }
