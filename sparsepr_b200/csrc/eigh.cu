@@ -122,6 +122,130 @@ sym_eig_kernel(const float* __restrict__ a_in, float* __restrict__ evals, float*
   }
 }
 
+// Same method for the two large sizes (n = 64, 128), restructured so a round
+// is one pass: with the pairs of a round (p_a, q_a) and their rotations J_a,
+// the rotated matrix J^T A J restricted to the 2x2 block (a, b) is
+// J_a^T A_ab J_b, so each thread rotates whole 2x2 blocks (both sides at
+// once; diagonal blocks get their exact zero off-diagonal) and the V columns
+// of its pairs in the same phase.  Rotation parameters are packed as one
+// float4 {c, s, p, q} per pair.  1024 threads, two barriers per round.
+constexpr int kEigBigThreads = 1024;
+
+template <int N>
+__global__ void __launch_bounds__(kEigBigThreads, 1)
+sym_eig_big_kernel(const float* __restrict__ a_in, float* __restrict__ evals, float* __restrict__ evecs,
+                   int max_sweeps, float rel_tol) {
+  constexpr int n = N, half = N / 2, ld = N + 1;
+  constexpr int kBlocks = half * half / kEigBigThreads;  // 2x2 blocks per thread
+  constexpr int kVItems = n * half / kEigBigThreads;     // (row, pair) V updates per thread
+  static_assert(kBlocks >= 1 && kVItems >= 1, "size not supported");
+  extern __shared__ float sh[];
+  float* A = sh;            // [n][ld]
+  float* V = sh + n * ld;   // [n][ld]
+  __shared__ float4 s_rot[half];
+  __shared__ int s_rank[N];
+  __shared__ float s_red[kEigBigThreads / 32][2];
+  __shared__ int s_stop;
+  const int64_t b = blockIdx.x;
+  const float* src = a_in + b * (int64_t)n * n;
+  const int tid = threadIdx.x;
+  for (int idx = tid; idx < n * n; idx += kEigBigThreads) {
+    const int i = idx / n, j = idx % n;
+    A[i * ld + j] = 0.5f * (src[i * n + j] + src[j * n + i]);
+    V[i * ld + j] = i == j ? 1.f : 0.f;
+  }
+  __syncthreads();
+  for (int sweep = 0; sweep < max_sweeps; ++sweep) {
+    float off = 0.f, tot = 0.f;
+    for (int idx = tid; idx < n * n; idx += kEigBigThreads) {
+      const int i = idx / n, j = idx % n;
+      const float x = A[i * ld + j];
+      tot += x * x;
+      if (i != j) off += x * x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      off += __shfl_xor_sync(0xffffffffu, off, o);
+      tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    }
+    if ((tid & 31) == 0) { s_red[tid >> 5][0] = off; s_red[tid >> 5][1] = tot; }
+    __syncthreads();
+    if (tid == 0) {
+      float so = 0.f, st = 0.f;
+      for (int w = 0; w < kEigBigThreads / 32; ++w) { so += s_red[w][0]; st += s_red[w][1]; }
+      s_stop = so <= rel_tol * rel_tol * st;
+    }
+    __syncthreads();
+    if (s_stop) break;
+    for (int round = 0; round < n - 1; ++round) {
+      if (tid < half) {
+        // Round-robin schedule: slot 0 holds index 0, slot i >= 1 holds
+        // 1 + (i - 1 + round) mod (n - 1); pair t is (slot t, slot n-1-t).
+        auto slot = [&](int i) { return i == 0 ? 0 : 1 + (i - 1 + round) % (n - 1); };
+        int p = slot(tid), q = slot(n - 1 - tid);
+        if (p > q) { const int t = p; p = q; q = t; }
+        const float apq = A[p * ld + q];
+        float c = 1.f, s = 0.f;
+        if (fabsf(apq) > 1e-30f) {
+          const float tau = (A[q * ld + q] - A[p * ld + p]) / (2.f * apq);
+          const float t = copysignf(1.f, tau) / (fabsf(tau) + sqrtf(1.f + tau * tau));
+          c = rsqrtf(1.f + t * t);
+          s = t * c;
+        }
+        s_rot[tid] = make_float4(c, s, __int_as_float(p), __int_as_float(q));
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kBlocks; ++k) {
+        const int z = tid + k * kEigBigThreads;
+        const int ia = z / half, ib = z % half;
+        const float4 ra = s_rot[ia], rb = s_rot[ib];
+        const int pa = __float_as_int(ra.z), qa = __float_as_int(ra.w);
+        const int pb = __float_as_int(rb.z), qb = __float_as_int(rb.w);
+        const float x00 = A[pa * ld + pb], x01 = A[pa * ld + qb], x10 = A[qa * ld + pb], x11 = A[qa * ld + qb];
+        // Rows (J_a^T): row p <- c row p - s row q, row q <- s row p + c row q.
+        const float y00 = ra.x * x00 - ra.y * x10, y01 = ra.x * x01 - ra.y * x11;
+        const float y10 = ra.y * x00 + ra.x * x10, y11 = ra.y * x01 + ra.x * x11;
+        // Columns (J_b): the same on columns p, q.
+        float z00 = rb.x * y00 - rb.y * y01, z01 = rb.y * y00 + rb.x * y01;
+        float z10 = rb.x * y10 - rb.y * y11, z11 = rb.y * y10 + rb.x * y11;
+        if (ia == ib) z01 = z10 = 0.f;  // the rotated pair's own off-diagonal
+        A[pa * ld + pb] = z00;
+        A[pa * ld + qb] = z01;
+        A[qa * ld + pb] = z10;
+        A[qa * ld + qb] = z11;
+      }
+#pragma unroll
+      for (int k = 0; k < kVItems; ++k) {
+        const int z = tid + k * kEigBigThreads;
+        const int i = z / half, ib = z % half;
+        const float4 rb = s_rot[ib];
+        const int pb = __float_as_int(rb.z), qb = __float_as_int(rb.w);
+        const float vp = V[i * ld + pb], vq = V[i * ld + qb];
+        V[i * ld + pb] = rb.x * vp - rb.y * vq;
+        V[i * ld + qb] = rb.y * vp + rb.x * vq;
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = tid; j < n; j += kEigBigThreads) {
+    const float lj = A[j * ld + j];
+    int rank = 0;
+    for (int i = 0; i < n; ++i) {
+      const float li = A[i * ld + i];
+      rank += (li < lj) || (li == lj && i < j);
+    }
+    evals[b * n + rank] = lj;
+    s_rank[j] = rank;
+  }
+  __syncthreads();
+  float* out = evecs + b * (int64_t)n * n;
+  for (int idx = tid; idx < n * n; idx += kEigBigThreads) {
+    const int i = idx / n, j = idx % n;
+    out[i * n + s_rank[j]] = V[i * ld + j];
+  }
+}
+
 }  // namespace spr
 
 using namespace spr;
@@ -138,6 +262,13 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
   const float tol = 1e-6f;
   const int smem = 2 * kEigMax * kEigLd * (int)sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
+  if (n == 64 || n == 128) {
+    const int big = 2 * n * (n + 1) * (int)sizeof(float);
+    auto kern = n == 64 ? sym_eig_big_kernel<64> : sym_eig_big_kernel<128>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+    kern<<<(unsigned)batch, kEigBigThreads, big, st>>>(a, evals, evecs, max_sweeps, tol);
+    return check_launch("sym_eig");
+  }
   switch (n) {
 #define SPR_EIG_CASE(NN)                                                                                      \
   case NN:                                                                                                    \
@@ -145,7 +276,7 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
     sym_eig_kernel<NN><<<(unsigned)batch, kEigThreads, smem, st>>>(a, evals, evecs, max_sweeps, tol);        \
     return check_launch("sym_eig");
     SPR_EIG_CASE(2) SPR_EIG_CASE(4) SPR_EIG_CASE(8) SPR_EIG_CASE(16) SPR_EIG_CASE(32) SPR_EIG_CASE(48)
-    SPR_EIG_CASE(64) SPR_EIG_CASE(96) SPR_EIG_CASE(128)
+    SPR_EIG_CASE(96)
 #undef SPR_EIG_CASE
     default:
       return fail(SPR_ERR_SHAPE, "sym_eig: n=%d not compiled (2,4,8,16,32,48,64,96,128)", n);

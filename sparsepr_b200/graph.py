@@ -1,4 +1,5 @@
-"""CUDA-graph capture of one SparsePR attention layer.
+"""CUDA-graph capture of one SparsePR attention layer, and a host-buffer front
+end that streams a layer through captured graphs in head chunks.
 
 Every step of ``sparse_attention`` is stream-ordered device work with no host
 synchronisation (fixed-density budgets), so a whole layer — role factors,
@@ -9,12 +10,18 @@ launch.  Inputs are copied into static device buffers before each replay.
 
 from __future__ import annotations
 
+import itertools
+
 import torch
 
+from . import kernels as K
 from .attention import sparse_attention
 from .n8_v6 import N8V6Config, N8V6Core
+from .synthetic import random_init_indices
 
-__all__ = ["GraphedSparseAttention"]
+__all__ = ["GraphedSparseAttention", "StreamedSparseAttention"]
+
+_SCOPE_IDS = itertools.count()
 
 
 class GraphedSparseAttention:
@@ -23,7 +30,9 @@ class GraphedSparseAttention:
     Each replay routes from scratch (a fresh core per call, like the first
     denoising step), so replays are independent of each other.
     ``selector_budget_mode`` must be ``fixed_density`` (the top-p mode reads
-    its density on the host).
+    its density on the host).  The graph's kernels use workspaces private to
+    this object, so different graphs may replay concurrently on different
+    streams.
     """
 
     def __init__(self, shape, config: N8V6Config, device: torch.device, warmup: int = 2):
@@ -36,9 +45,27 @@ class GraphedSparseAttention:
         self.v = torch.zeros_like(self.q)
         self.graph = None
         self._warmup = warmup
+        self._scope = f"graph{next(_SCOPE_IDS)}"
+        # Cold-start centroid rows: a static input of the graph (default: the
+        # config's own draw for this batch; load(..., init_rows) selects others).
+        b, h, n, _d = shape
+        self.k_init = random_init_indices(b * h, n, config.num_k_centroids, config.kmeans_init_seed).to(device)
+        self.q_init = random_init_indices(b * h, n, config.num_q_centroids, config.kmeans_init_seed + 1).to(device)
+
+    def init_rows(self, offset: int, total: int):
+        """Device copies of rows ``[offset, offset + BH)`` of the cold-start draw
+        for ``total`` problems (pass them to ``load``)."""
+        bh = self.k_init.shape[0]
+        n = self.q.shape[2]
+        cfg = self.config
+        k = random_init_indices(total, n, cfg.num_k_centroids, cfg.kmeans_init_seed)[offset:offset + bh]
+        q = random_init_indices(total, n, cfg.num_q_centroids, cfg.kmeans_init_seed + 1)[offset:offset + bh]
+        return k.to(self.device), q.to(self.device)
 
     def _run(self):
-        return sparse_attention(self.q, self.k, self.v, N8V6Core(self.config))
+        with K.workspace_scope(self._scope):
+            core = N8V6Core(self.config, init_indices=(self.k_init, self.q_init))
+            return sparse_attention(self.q, self.k, self.v, core)
 
     def capture(self):
         """Warm up on a side stream (caches workspaces and index constants), then capture."""
@@ -54,11 +81,15 @@ class GraphedSparseAttention:
             self.out, self.density, self.info = self._run()
         return self
 
-    def load(self, q, k, v):
-        """Copy inputs (device or pinned host tensors) into the static buffers."""
+    def load(self, q, k, v, init_rows=None):
+        """Copy inputs (device or pinned host tensors) into the static buffers;
+        ``init_rows`` = a pair from ``init_rows()`` (device tensors)."""
         self.q.copy_(q, non_blocking=True)
         self.k.copy_(k, non_blocking=True)
         self.v.copy_(v, non_blocking=True)
+        if init_rows is not None:
+            self.k_init.copy_(init_rows[0], non_blocking=True)
+            self.q_init.copy_(init_rows[1], non_blocking=True)
 
     def replay(self):
         if self.graph is None:
@@ -69,3 +100,56 @@ class GraphedSparseAttention:
     def __call__(self, q, k, v):
         self.load(q, k, v)
         return self.replay()
+
+
+class StreamedSparseAttention:
+    """SparsePR layer on host tensors, streamed through captured graphs by head chunks.
+
+    ``__call__(hq, hk, hv, hout)`` takes pinned host ``[B,H,N,D]`` bf16
+    tensors and writes the repaired output into the pinned host ``hout``.
+    Heads are independent in every step of the layer, so the heads are cut
+    into chunks of ``heads_per_chunk``; chunk i's host-to-device copy, graph
+    replay and device-to-host copy are queued on stream ``i % slots``.  The
+    copy engines then move one chunk while the SMs compute another.  Each
+    chunk starts its k-means from its rows of the all-heads cold-start draw,
+    and no step of the layer mixes heads, so the result equals one
+    ``GraphedSparseAttention`` call over all heads.
+    """
+
+    def __init__(self, shape, config: N8V6Config, device: torch.device, heads_per_chunk: int = 8,
+                 slots: int = 2, warmup: int = 2):
+        b, h, n, d = shape
+        if h % heads_per_chunk:
+            raise ValueError(f"{h} heads do not split into chunks of {heads_per_chunk}")
+        if b != 1:
+            raise ValueError("streamed layers take B=1 (one [H,N,D] problem set per call)")
+        self.shape = tuple(shape)
+        self.device = device
+        self.chunks = [(h0, h0 + heads_per_chunk) for h0 in range(0, h, heads_per_chunk)]
+        nslots = min(slots, len(self.chunks))
+        self.slots = [GraphedSparseAttention((b, heads_per_chunk, n, d), config, device, warmup)
+                      for _ in range(nslots)]
+        self.streams = [torch.cuda.Stream(device) for _ in range(nslots)]
+        # Each chunk's rows of the all-heads cold-start draw (device, loaded per replay).
+        self.init = [self.slots[0].init_rows(h0, h) for h0, _h1 in self.chunks]
+
+    def capture(self):
+        for g in self.slots:
+            g.capture()
+        return self
+
+    def __call__(self, hq, hk, hv, hout):
+        if any(g.graph is None for g in self.slots):
+            self.capture()
+        cur = torch.cuda.current_stream(self.device)
+        for st in self.streams:
+            st.wait_stream(cur)
+        for i, (h0, h1) in enumerate(self.chunks):
+            g = self.slots[i % len(self.slots)]
+            with torch.cuda.stream(self.streams[i % len(self.slots)]):
+                g.load(hq[:, h0:h1], hk[:, h0:h1], hv[:, h0:h1], self.init[i])
+                g.graph.replay()
+                hout[:, h0:h1].copy_(g.out, non_blocking=True)
+        for st in self.streams:
+            cur.wait_stream(st)
+        return hout

@@ -7,6 +7,8 @@ stream.  There is no CPU path: non-CUDA inputs raise ``RuntimeError``.
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from . import _lib
@@ -44,9 +46,27 @@ def _contig(name: str, t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+_SCOPE = [""]
+
+
+@contextlib.contextmanager
+def workspace_scope(name: str):
+    """Workspaces requested inside the block are private to ``name``.
+
+    Work that may run concurrently (two captured graphs replayed on different
+    streams) must not share scratch buffers; each graph captures under its own
+    scope."""
+    prev = _SCOPE[0]
+    _SCOPE[0] = name
+    try:
+        yield
+    finally:
+        _SCOPE[0] = prev
+
+
 def workspace(dev: torch.device, nbytes: int, tag: str = "default") -> torch.Tensor:
-    """Caller-owned scratch, cached per (device, tag) and grown on demand."""
-    key = (dev.type, dev.index, tag)
+    """Caller-owned scratch, cached per (device, scope, tag) and grown on demand."""
+    key = (dev.type, dev.index, _SCOPE[0], tag)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
@@ -81,7 +101,7 @@ def kmeans_assign(x: torch.Tensor, centroids: torch.Tensor, precision: str = "tf
 
 def kmeans_error_code(dev: torch.device) -> int:
     """Device status word of the last k-means call on ``dev`` (0 = ok).  Synchronises; for tests."""
-    ws = _WS.get((dev.type, dev.index, "kmeans"))
+    ws = _WS.get((dev.type, dev.index, _SCOPE[0], "kmeans"))
     if ws is None:
         return 0
     torch.cuda.synchronize(dev)
@@ -227,7 +247,7 @@ def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids
 def attention_error_code(dev: torch.device) -> int:
     """Device status word of the last block-sparse attention launch on ``dev``
     (0 = ok, else the bounded wait that gave up).  Synchronises; for tests."""
-    ws = _WS.get((dev.type, dev.index, "attn"))
+    ws = _WS.get((dev.type, dev.index, _SCOPE[0], "attn"))
     if ws is None:
         return 0
     torch.cuda.synchronize(dev)

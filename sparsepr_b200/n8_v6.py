@@ -387,9 +387,14 @@ class N8V6Core:
     warm subspace iteration (``operator_kmeans.py:221-477``) is not implemented.
     """
 
-    def __init__(self, config: N8V6Config):
+    def __init__(self, config: N8V6Config, init_indices: tuple[torch.Tensor, torch.Tensor] | None = None):
+        """``init_indices`` (extension): device tensors ``(k_idx [BH,Ck], q_idx [BH,Cq])``
+        of cold-start centroid rows, used instead of ``random_init_indices``
+        (a caller running a subset of the heads passes its rows of the full
+        draw, so its results match a call over all heads)."""
         config.validate()
         self.config = config
+        self.init_indices = init_indices
         self.q_centroids: torch.Tensor | None = None
         self.k_centroids: torch.Tensor | None = None
         self.v_centroids: torch.Tensor | None = None
@@ -407,7 +412,7 @@ class N8V6Core:
         return self.q_centroids is not None
 
     def reset(self) -> None:
-        self.__init__(self.config)
+        self.__init__(self.config, self.init_indices)
 
     # -- route ---------------------------------------------------------------
     def route(self, q_video, k_video, v_video, *, gqa_group_size: int = 1, always_attended_keys: int = 0,
@@ -455,7 +460,8 @@ class N8V6Core:
             if k_init_features is None and warm:
                 k_init_features = torch.bmm(self.k_centroids, k_factor) / k_scale
         if k_init_features is None:
-            idx = _init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev)
+            idx = (self.init_indices[0] if self.init_indices is not None
+                   else _init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev))
             k_init_features = torch.gather(k_feat, 1, idx.unsqueeze(-1).expand(-1, -1, k_feat.shape[-1]))
         k_labels, _kc, k_sizes, k_off, k_order, k_it = K.kmeans_lloyd(k_feat, k_init_features, iters, cfg.kmeans_tol,
                                                                      precision=cfg.kmeans_precision)
@@ -490,7 +496,8 @@ class N8V6Core:
                 qi = torch.bmm(self.q_centroids, q_factor)
                 q_init_features = qi / qi.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)
         if q_init_features is None:
-            idx = _init_indices(bh, tokens, cfg.num_q_centroids, cfg.kmeans_init_seed + 1, dev)
+            idx = (self.init_indices[1] if self.init_indices is not None
+                   else _init_indices(bh, tokens, cfg.num_q_centroids, cfg.kmeans_init_seed + 1, dev))
             q_init_features = torch.gather(q_feat, 1, idx.unsqueeze(-1).expand(-1, -1, q_feat.shape[-1]))
         q_labels, _qc, q_sizes, q_off, q_order, q_it = K.kmeans_lloyd(q_feat, q_init_features, iters, cfg.kmeans_tol,
                                                                      precision=cfg.kmeans_precision)

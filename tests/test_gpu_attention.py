@@ -213,3 +213,26 @@ def test_graph_replay_matches_eager(cuda):
     torch.cuda.synchronize()
     assert torch.equal(got, again)
     _close(got.view(2, -1, 128), eager.view(2, -1, 128))
+
+
+def test_streamed_host_layer_matches_all_heads_graph(cuda):
+    """Head-chunked streaming from pinned host buffers (two slots, copies on the
+    slot streams) gives the output of one captured graph over all heads: each
+    chunk starts k-means from its rows of the all-heads cold-start draw."""
+    from sparsepr_b200.graph import GraphedSparseAttention, StreamedSparseAttention
+
+    cfg = _cfg()
+    q, k, v = synthetic_qkv(6, 128, (4, 8, 16), dtype=torch.bfloat16)
+    ref = GraphedSparseAttention(q.shape, cfg, cuda).capture()(q.to(cuda), k.to(cuda), v.to(cuda)).cpu()
+    hq, hk, hv = (t.pin_memory() for t in (q, k, v))
+    hout = torch.empty_like(hq).pin_memory()
+    s = StreamedSparseAttention(q.shape, cfg, cuda, heads_per_chunk=2, slots=2).capture()
+    for _ in range(2):  # the second call reuses both slots' graphs
+        hout.zero_()
+        s(hq, hk, hv, hout)
+        torch.cuda.synchronize()
+        # Batched torch GEMMs inside the route may round differently at another
+        # batch size, so compare with the layer tolerance; most heads match exactly.
+        _close(hout.view(6, -1, 128), ref.view(6, -1, 128))
+        same = sum(torch.equal(hout[0, h], ref[0, h]) for h in range(6))
+        assert same >= 3, same
