@@ -332,8 +332,8 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
-    ap.add_argument("--e2e-chunk", type=int, default=10, help="heads per streamed chunk in the e2e measurement")
-    ap.add_argument("--e2e-slots", type=int, default=2, help="concurrent graph slots (streams) in the e2e measurement")
+    ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
+    ap.add_argument("--e2e-slots", type=int, default=8, help="concurrent graph slots (streams) in the e2e measurement")
     ap.add_argument("--kernel-table", action="store_true",
                     help="print per-kernel device times of one layer (torch profiler) instead of the bench line")
     args = ap.parse_args()

@@ -1,31 +1,41 @@
 // Block-sparse flash attention over kept (query-cluster, key-cluster) pairs on
 // the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// Work unit (one CTA): a 128-row tile of one query cluster of the
-// cluster-sorted Q.  Its keys are the concatenated token runs of the selected
-// key clusters of the cluster-sorted K/V, consumed in 128-key tiles; only the
-// last tile of a cluster can be partial, so masking is a column bound.
+// Work unit (one CTA): up to two 128-row query tiles A and B (256 consecutive
+// rows) of one query cluster of the cluster-sorted Q.  Both tiles attend to
+// the same keys: the concatenated token runs of the cluster's selected key
+// clusters in the cluster-sorted K/V, consumed in 128-key tiles (only the last
+// tile can be partial, so masking is a column bound).  Every K/V tile is
+// loaded once and used by both query tiles.
 //
-// Warp roles (256 threads):
-//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t).  Loads the
-//              S row from TMEM, online softmax in base 2 with a lazily
-//              updated running max, writes P (bf16) to tensor memory, rescales
-//              the O accumulator in TMEM when the max moves, and finally
-//              normalises O and stores the row (through q_order: the inverse
-//              permute is fused into the store).
-//   warp 4     MMA issuer (one thread): S(j) = Q K_j^T into one of two TMEM S
-//              buffers, O += P(j) V_j into the TMEM O accumulator with P read
-//              from tensor memory (no shared-memory round trip for P).
-//   warps 5-8  loaders: warps 5-6 gather K rows, warps 7-8 V rows, each into
-//              its own 2-stage ring with 16-byte cp.async.  K stage j is freed
-//              as soon as S(j) is done and V stage j when PV(j) is done, so
-//              the gather latency of tile j+2 hides behind the MMAs of tiles
-//              j and j+1.  The selected clusters' runs (start, prefix length)
+// Warp roles (384 threads):
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread t of a
+//              group owns query row t (= TMEM lane t).  Loads the S row from
+//              TMEM, online softmax in base 2 with a lazily updated running
+//              max, writes P (bf16) over the first 64 columns of its own S
+//              region, rescales the O accumulator in TMEM when the max moves,
+//              and finally normalises O and stores the row (through q_order:
+//              the inverse permute is fused into the store).
+//   warp 8     MMA issuer (one thread).  Order per key tile j:
+//                PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs.  PV reads P from tensor memory.
+//   warps 9-11 loaders: warps 9-10 gather K rows [64w, 64w+64) of each key
+//              tile, warp 11 all V rows, each into a 2-stage ring with 16-byte
+//              cp.async.  The selected clusters' runs (start, prefix length)
 //              are staged in shared memory once per CTA; each loader lane
-//              resolves one key slot by binary search, and each warp
-//              instruction moves two full 256-byte rows.
-// TMEM: columns [0,128) and [128,256) are the two S buffers, [256,384) is O,
-// [384,448) is P (bf16 pairs, one 32-bit column per two keys).
+//              walks them with a forward cursor, and each warp instruction
+//              moves two full 256-byte rows.
+// TMEM: tile X in {A, B} owns columns [256X, 256X+128) for S(j) (P(j) over its
+// first 64 columns, one 32-bit column per two keys) and [256X+128, 256X+256)
+// for O.  tcgen05.commit tracks every earlier MMA of the issuing thread, so
+// when S_X(j) is reported complete, PV_X(j-1) is complete too: the softmax may
+// then rescale O_X and overwrite P_X without another barrier.  S_X(j+1) is
+// issued after PV_X(j), which has read P_X by then (MMAs of one thread execute
+// in issue order).
+// The softmax arithmetic is the per-tile critical path: it uses packed fp32
+// pair instructions (fma/add .f32x2), the three-input max, and takes one
+// exponential in four off the MUFU unit (ex2_fma2).
 // Operand tiles use the canonical 128-byte-swizzled K-major layout; V is the
 // MN-major B operand of the PV product.
 #include "tc_common.cuh"
@@ -37,19 +47,65 @@ using namespace tc;
 constexpr int kD = 128;
 constexpr int kTileM = 128;
 constexpr int kTileN = 128;
-constexpr int kSoftmaxThreads = 128;
-constexpr int kLoaderThreads = 128;
-constexpr int kThreadsTc = 288;
+constexpr int kPairRows = 2 * kTileM;   // query rows per CTA
+constexpr int kSoftmaxThreads = 128;    // per query tile
+constexpr int kThreadsTc = 384;
 constexpr int kMaxRuns = 2048;  // key clusters per problem (ck) this kernel accepts
 constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
-constexpr int kSmemTc = 1024 /*align slack*/ + kTileBytes /*Q*/ + 4 * kTileBytes /*K,V x2*/;
+constexpr int kSmemTc = 1024 /*align slack*/ + 2 * kTileBytes /*Q_A, Q_B*/ + 4 * kTileBytes /*K,V x2*/;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 1);
 
 enum : int { kErrTimeoutLoad = 1, kErrTimeoutMma = 2, kErrTimeoutSoftmax = 3 };
 
-// err[0] = 0, tile_start[b][c] = first 128-row tile of query cluster c in
-// problem b (exclusive prefix of ceil(size/128)); tile_start[b][cq] = total.
+// Packed fp32 pairs (sm_100 f32x2 instructions) and the three-input max.
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of scores on the FMA pipe, for the share of the softmax
+// exponentials taken off the MUFU unit.  Cody-Waite split x = n + f with
+// n = round(x) from the low mantissa bits of x + 1.5*2^23 and |f| <= 1/2;
+// 2^f from a cubic with constant term 1 fitted for minimum relative error on
+// [-1/2, 1/2] (max 1.0e-4, below the 2^-9 rounding of P to bf16); 2^n added
+// to the exponent field.  Inputs below -125 (including -inf) give 2^-125.
+__device__ __forceinline__ void ex2_fma2(float x0, float x1, float& p0, float& p1) {
+  const unsigned long long xc = pk2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const unsigned long long mg = pk2(12582912.f, 12582912.f);
+  const unsigned long long t = add2(xc, mg);
+  const unsigned long long f = add2(xc, fma2(t, pk2(-1.f, -1.f), mg));  // x - (t - magic)
+  unsigned long long q = fma2(f, pk2(0.055008821f, 0.055008821f), pk2(0.24221078f, 0.24221078f));
+  q = fma2(q, f, pk2(0.69328290f, 0.69328290f));
+  q = fma2(q, f, pk2(1.f, 1.f));
+  float q0, q1, t0, t1;
+  up2(q, q0, q1);
+  up2(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+// err[0] = 0, tile_start[b][c] = first 256-row unit of query cluster c in
+// problem b (exclusive prefix of ceil(size/256)); tile_start[b][cq] = total.
 __global__ void tile_table_kernel(const int32_t* __restrict__ q_offsets, int cq, int32_t* __restrict__ tile_start,
                                   int* __restrict__ err) {
   const int64_t b = blockIdx.x;
@@ -59,7 +115,7 @@ __global__ void tile_table_kernel(const int32_t* __restrict__ q_offsets, int cq,
   for (int c = 0; c < cq; ++c) {
     tile_start[b * (cq + 1) + c] = acc;
     const int32_t sz = q_offsets[b * (cq + 1) + c + 1] - q_offsets[b * (cq + 1) + c];
-    acc += (sz + kTileM - 1) / kTileM;
+    acc += (sz + kPairRows - 1) / kPairRows;
   }
   tile_start[b * (cq + 1) + cq] = acc;
 }
@@ -72,31 +128,33 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
                             int64_t nq, int64_t nk, int cq, int ck, const int32_t* __restrict__ q_order,
                             __nv_bfloat16* __restrict__ out, float scale_log2, int* __restrict__ err) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t bar_k_full[2], bar_k_empty[2], bar_v_full[2], bar_v_empty[2], bar_s_full[2], bar_p_full,
-      bar_o_done;
+  __shared__ uint64_t bar_k_full[2], bar_k_empty[2], bar_v_full[2], bar_v_empty[2], bar_s_full[2], bar_p_full[2],
+      bar_o_done[2];
   __shared__ uint32_t s_tmem;
   __shared__ int32_t s_run_start[kMaxRuns];
   __shared__ int32_t s_run_end[kMaxRuns + 1];  // inclusive prefix of run lengths
   __shared__ int s_total;
 
   const int64_t b = blockIdx.y;
-  const int tile = blockIdx.x;
+  const int unit = blockIdx.x;
   const int32_t* ts = tile_start + b * (cq + 1);
-  if (tile >= ts[cq]) return;  // block-uniform, before any barrier or TMEM use
-  int lo = 0, hi = cq - 1;     // query cluster owning the tile: last c with ts[c] <= tile
+  if (unit >= ts[cq]) return;  // block-uniform, before any barrier or TMEM use
+  int lo = 0, hi = cq - 1;     // query cluster owning the unit: last c with ts[c] <= unit
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (ts[mid] <= tile) lo = mid; else hi = mid - 1;
+    if (ts[mid] <= unit) lo = mid; else hi = mid - 1;
   }
   const int c = lo;
   const int32_t qbeg = q_offsets[b * (cq + 1) + c];
   const int32_t qend = q_offsets[b * (cq + 1) + c + 1];
-  const int32_t row0 = qbeg + (tile - ts[c]) * kTileM;
-  const int rows = min(kTileM, qend - row0);
+  const int32_t row0 = qbeg + (unit - ts[c]) * kPairRows;
+  const int rows_a = min(kTileM, qend - row0);
+  const int rows_b = max(0, min(kTileM, qend - row0 - kTileM));
+  const bool has_b = rows_b > 0;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kTileBytes;        // 2 stages
+  uint8_t* sQ = smem;                   // Q_A, Q_B
+  uint8_t* sK = sQ + 2 * kTileBytes;    // 2 stages
   uint8_t* sV = sK + 2 * kTileBytes;    // 2 stages
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -109,18 +167,18 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar_k_full[i], kLoaderThreads / 2);
-      mbar_init(&bar_v_full[i], kLoaderThreads / 2);
+      mbar_init(&bar_k_full[i], 64);  // two K loader warps
+      mbar_init(&bar_v_full[i], 32);  // one V loader warp
       mbar_init(&bar_k_empty[i], 1);
       mbar_init(&bar_v_empty[i], 1);
       mbar_init(&bar_s_full[i], 1);
+      mbar_init(&bar_p_full[i], kSoftmaxThreads);
+      mbar_init(&bar_o_done[i], 1);
     }
-    mbar_init(&bar_p_full, kSoftmaxThreads);
-    mbar_init(&bar_o_done, 1);
     mbar_fence_init();
   }
-  if (warp == 4) tmem_alloc<512>(&s_tmem);
-  if (warp == 5) {  // run table of the selected key clusters: start row and prefix length
+  if (warp == 8) tmem_alloc<512>(&s_tmem);
+  if (warp == 9) {  // run table of the selected key clusters: start row and prefix length
     int carry = 0;
     for (int base = 0; base < nsel; base += 32) {
       const int i = base + lane;
@@ -144,11 +202,12 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     }
     if (lane == 0) s_total = carry;
   }
-  // Q tile (all threads), zero rows past the cluster end.
-  for (int i = tid; i < kTileM * 16; i += kThreadsTc) {
-    const int r = i >> 4, ch = i & 15;
-    const bool ok = r < rows;
-    cp_async16(smem_addr(sQ) + sw128_off(r, ch, kTileM), qb + (int64_t)(row0 + (ok ? r : 0)) * kD + ch * 8, ok);
+  // Q tiles (all threads), zero rows past the cluster end.
+  for (int i = tid; i < 2 * kTileM * 16; i += kThreadsTc) {
+    const int t = i >> 11, r = (i >> 4) & 127, ch = i & 15;
+    const bool ok = r < (t ? rows_b : rows_a);
+    cp_async16(smem_addr(sQ + t * kTileBytes) + sw128_off(r, ch, kTileM),
+               qb + (int64_t)(row0 + t * kTileM + (ok ? r : 0)) * kD + ch * 8, ok);
   }
   cp_async_commit();
   cp_async_wait_all();
@@ -160,44 +219,46 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   const int total = s_total;
   const int ntiles = (total + kTileN - 1) / kTileN;
 
-  if (warp >= 5) {
+  if (warp >= 9) {
     // ------------------------------------------------------------ loaders
-    const bool is_v = warp >= 7;                 // warps 5-6: K, warps 7-8: V
-    const int gw = (warp - 5) & 1;               // rows [64*gw, 64*gw+64) of each key tile
+    const bool is_v = warp == 11;
+    const int nsub = is_v ? 4 : 2;                // 32-row groups handled by this warp
+    const int band = is_v ? 0 : (warp - 9) * 64;  // first row of this warp's band
     const __nv_bfloat16* srcb = is_v ? vb : kb;
     uint8_t* ring = is_v ? sV : sK;
     uint64_t* full = is_v ? bar_v_full : bar_k_full;
     uint64_t* empty = is_v ? bar_v_empty : bar_k_empty;
     const int half = lane >> 4, ch = lane & 15;
-    // Per-lane run cursors: slot g = j*128 + 64*gw + 32*sub + lane grows by 128
+    // Per-lane run cursors: slot g = j*128 + band + 32*sub + lane grows by 128
     // per tile, so each cursor only walks forward over the runs it passes.
-    int cur[2] = {0, 0};
+    int cur[4] = {0, 0, 0, 0};
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      int src[2];
+      int src[4];
 #pragma unroll
-      for (int sub = 0; sub < 2; ++sub) {
-        const int g = j * kTileN + gw * 64 + sub * 32 + lane;
+      for (int sub = 0; sub < 4; ++sub) {
         src[sub] = -1;
-        if (g < total) {
+        const int g = j * kTileN + band + sub * 32 + lane;
+        if (sub < nsub && g < total) {
           while (s_run_end[cur[sub]] <= g) ++cur[sub];
           const int prev = cur[sub] > 0 ? s_run_end[cur[sub] - 1] : 0;
           src[sub] = s_run_start[cur[sub]] + (g - prev);
         }
       }
-      if (j >= 2) mbar_wait(&empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad);
+      if (j >= 2 && !mbar_wait(&empty[st], ((j >> 1) - 1) & 1, err, kErrTimeoutLoad)) break;
       // Swizzled destination of (row r, chunk ch): rows of one warp step differ
       // only in (r & 7), fixed per unrolled iteration.
       const uint32_t dst = smem_addr(ring + st * kTileBytes) + (uint32_t)(ch >> 3) * (kTileN * 128) +
-                           (uint32_t)(gw * 64) * 128;
+                           (uint32_t)band * 128;
       const __nv_bfloat16* colp = srcb + ch * 8;
 #pragma unroll
-      for (int sub = 0; sub < 2; ++sub) {
+      for (int sub = 0; sub < 4; ++sub) {
+        if (sub >= nsub) break;  // warp-uniform
 #pragma unroll
         for (int pr = 0; pr < 16; ++pr) {  // two rows per instruction: lanes 0-15 row 2pr, 16-31 row 2pr+1
           const int rl = 2 * pr + half;
           const int rsrc = __shfl_sync(0xffffffffu, src[sub], rl);
-          const int rr = sub * 32 + rl;  // row within this warp's 64-row band (band start is 8-aligned)
+          const int rr = sub * 32 + rl;  // row within this warp's band (band start is 8-aligned)
           const uint32_t o = (uint32_t)rr * 128 + ((uint32_t)((ch & 7) ^ (rr & 7)) << 4);
           cp_async16(dst + o, colp + (uint32_t)max(rsrc, 0) * (uint32_t)kD, rsrc >= 0);
         }
@@ -205,132 +266,155 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       cp_async_arrive(&full[st]);  // completes when this lane's copies have landed
     }
     cp_async_wait_all();
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && ntiles > 0) {
-      const uint32_t tS[2] = {tmem, tmem + 128};
-      const uint32_t tO = tmem + 256, tP = tmem + 384;
       const uint32_t aq = smem_addr(sQ);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&bar_k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t bk = smem_addr(sK + st * kTileBytes);
+      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T (K_j resident)
+        const uint32_t bk = smem_addr(sK + (j & 1) * kTileBytes);
+        const uint32_t ax = aq + x * kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {  // K-major: 32 B per 16-element step, second half +16 KB
           const uint32_t koff = (kk >> 2) * (kTileM * 128) + (kk & 3) * 32;
-          mma_f16(tS[st], sw128_desc(aq + koff, 16, 1024), sw128_desc(bk + koff, 16, 1024), kIdescQK, kk > 0);
+          mma_f16(tmem + 256 * x, sw128_desc(ax + koff, 16, 1024), sw128_desc(bk + koff, 16, 1024), kIdescQK,
+                  kk > 0);
         }
-        mma_commit(&bar_s_full[st]);
-        mma_commit(&bar_k_empty[st]);
-        return true;
+        mma_commit(&bar_s_full[x]);
       };
-      bool ok = issue_s(0);
-      if (ok && ntiles > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j & 1;
-        if (!(ok = mbar_wait(&bar_p_full, j & 1, err, kErrTimeoutMma))) break;
-        if (!(ok = mbar_wait(&bar_v_full[st], (j >> 1) & 1, err, kErrTimeoutMma))) break;
-        tc_fence_after();
-        const uint32_t bv = smem_addr(sV + st * kTileBytes);
+      auto issue_pv = [&](int x, int j) {  // O_x += P_x(j) V_j, P_x from tensor memory
+        const uint32_t bv = smem_addr(sV + (j & 1) * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk) {  // 16 keys per step
-          const uint32_t voff = kk * 2048;  // V is MN-major: 16 rows = 2 x 1024 B
-          mma_f16_ts(tO, tP + kk * 8, sw128_desc(bv + voff, kTileN * 128, 1024), kIdescPV,  // 16 keys = 8 columns
-                     (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kTileN / 16; ++kk) {  // 16 keys per step = 8 TMEM columns of P
+          const uint32_t voff = kk * 2048;         // V is MN-major: 16 rows = 2 x 1024 B
+          mma_f16_ts(tmem + 256 * x + 128, tmem + 256 * x + kk * 8, sw128_desc(bv + voff, kTileN * 128, 1024),
+                     kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&bar_o_done);
-        mma_commit(&bar_v_empty[st]);
-        if (j + 2 < ntiles) ok = issue_s(j + 2);
+      };
+      bool ok = mbar_wait(&bar_k_full[0], 0, err, kErrTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has_b) issue_s(1, 0);
+        mma_commit(&bar_k_empty[0]);
       }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const bool next = j + 1 < ntiles;
+        if (!(ok = mbar_wait(&bar_v_full[j & 1], (j >> 1) & 1, err, kErrTimeoutMma))) break;
+        if (next && !(ok = mbar_wait(&bar_k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, kErrTimeoutMma))) break;
+        if (!(ok = mbar_wait(&bar_p_full[0], j & 1, err, kErrTimeoutMma))) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (next) issue_s(0, j + 1);
+        if (has_b) {
+          if (!(ok = mbar_wait(&bar_p_full[1], j & 1, err, kErrTimeoutMma))) break;
+          tc_fence_after();
+          issue_pv(1, j);
+          if (next) issue_s(1, j + 1);
+        }
+        mma_commit(&bar_v_empty[j & 1]);
+        if (next) mma_commit(&bar_k_empty[(j + 1) & 1]);
+      }
+      mma_commit(&bar_o_done[0]);
+      mma_commit(&bar_o_done[1]);
     }
-  } else {
+  } else if (warp < 4 || has_b) {
     // ------------------------------------------------------------ softmax (thread = row)
-    const int row = tid;  // TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int x = warp >> 2;  // query tile
+    const int rows = x ? rows_b : rows_a;
+    const int row = tid & 127;  // TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + 256 * x, tO = tS + 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s_full[st], (j >> 1) & 1, err, kErrTimeoutSoftmax));
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_s_full[x], j & 1, err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
       float s[kTileN];
-      tmem_ld64(tmem + lane_base + st * 128, s);
-      tmem_ld64(tmem + lane_base + st * 128 + 64, s + 64);
+      tmem_ld32_async(tS, s);  // four loads in flight, one wait
+      tmem_ld32_async(tS + 32, s + 32);
+      tmem_ld32_async(tS + 64, s + 64);
+      tmem_ld32_async(tS + 96, s + 96);
+      tmem_wait_ld();
+      reg_fence32(s);
+      reg_fence32(s + 32);
+      reg_fence32(s + 64);
+      reg_fence32(s + 96);
       const int valid = total - j * kTileN;
       if (valid < kTileN) {  // only the last tile of a cluster is partial (warp-uniform)
 #pragma unroll
-        for (int x = 0; x < kTileN; ++x) s[x] = x < valid ? s[x] : -INFINITY;
+        for (int i = 0; i < kTileN; ++i) s[i] = i < valid ? s[i] : -INFINITY;
       }
-      float m4[4] = {s[0], s[1], s[2], s[3]};
+      float m8[8];  // eight independent max chains, two scores per instruction
 #pragma unroll
-      for (int x = 4; x < kTileN; x += 4) {
-        m4[0] = fmaxf(m4[0], s[x]);
-        m4[1] = fmaxf(m4[1], s[x + 1]);
-        m4[2] = fmaxf(m4[2], s[x + 2]);
-        m4[3] = fmaxf(m4[3], s[x + 3]);
+      for (int cc = 0; cc < 8; ++cc) m8[cc] = fmaxf(s[2 * cc], s[2 * cc + 1]);
+#pragma unroll
+      for (int i = 16; i < kTileN; i += 16) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) m8[cc] = max3(m8[cc], s[i + 2 * cc], s[i + 2 * cc + 1]);
       }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
+      const float mx = max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7])) * scale_log2;
       // Lazy max: keep the running max unless it grew by more than 8 (base 2).
       float alpha = 1.f;
       if (mx > m_run + 8.f || m_run == -INFINITY) {
         alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
         m_run = mx;
       }
-      const float neg_m = -m_run;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      const unsigned long long sc2 = pk2(scale_log2, scale_log2), nm2 = pk2(-m_run, -m_run);
+      unsigned long long sum2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial sums (+0.0f pairs)
       uint32_t pk[kTileN / 2];
 #pragma unroll
-      for (int x = 0; x < kTileN; x += 2) {
-        const float p0 = ex2(fmaf(s[x], scale_log2, neg_m));
-        const float p1 = ex2(fmaf(s[x + 1], scale_log2, neg_m));
-        sum4[(x >> 1) & 3] += p0 + p1;
-        __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
-        pk[x >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      for (int i = 0; i < kTileN; i += 2) {
+        float x0, x1, p0, p1;
+        up2(fma2(pk2(s[i], s[i + 1]), sc2, nm2), x0, x1);
+        if ((i & 7) == 0) {  // one pair in four on the FMA pipe, the rest on MUFU
+          ex2_fma2(x0, x1, p0, p1);
+        } else {
+          p0 = ex2(x0);
+          p1 = ex2(x1);
+        }
+        sum2[(i >> 1) & 3] = add2(sum2[(i >> 1) & 3], pk2(p0, p1));
+        __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+        pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      l_run = l_run * alpha + sum;
-      if (j > 0) {
-        // PV(j-1) must be complete before O is rescaled and P is overwritten.
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_o_done, (j - 1) & 1, err, kErrTimeoutSoftmax));
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // warp-uniform: TMEM ld/st are warp-collective
-          float o[32];
+      float a0, a1, b0, b1;
+      up2(add2(sum2[0], sum2[1]), a0, a1);
+      up2(add2(sum2[2], sum2[3]), b0, b1);
+      l_run = l_run * alpha + ((a0 + a1) + (b0 + b1));
+      // PV_x(j-1) is complete (S_x(j) completed after it): O_x may be rescaled.
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // warp-uniform: TMEM ld/st are warp-collective
+        float o[32];
 #pragma unroll
-          for (int cb = 0; cb < 4; ++cb) {
-            tmem_ld32(tmem + lane_base + 256 + cb * 32, o);
+        for (int cb = 0; cb < 4; ++cb) {
+          tmem_ld32(tO + cb * 32, o);
 #pragma unroll
-            for (int x = 0; x < 32; ++x) o[x] *= alpha;
-            tmem_st32(tmem + lane_base + 256 + cb * 32, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + cb * 32, o);
         }
       }
-      // P(j) replaces P(j-1), which PV(j-1) (complete, waited above) has read.
-      tmem_st32(tmem + lane_base + 384, reinterpret_cast<const float*>(pk));
-      tmem_st32(tmem + lane_base + 384 + 32, reinterpret_cast<const float*>(pk + 32));
+      // P(j) over the first 64 columns of S(j) (already loaded above).
+      tmem_st32(tS, reinterpret_cast<const float*>(pk));
+      tmem_st32(tS + 32, reinterpret_cast<const float*>(pk + 32));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar_p_full);
+      mbar_arrive(&bar_p_full[x]);
     }
     // Epilogue: O / l, bf16, stored through the inverse permutation.
-    if (ok && ntiles > 0) ok = mbar_wait(&bar_o_done, (ntiles - 1) & 1, err, kErrTimeoutSoftmax);
+    if (ok && ntiles > 0) ok = mbar_wait(&bar_o_done[x], 0, err, kErrTimeoutSoftmax);
     const bool have = __all_sync(0xffffffffu, ok && ntiles > 0);
     tc_fence_after();
     const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
-    const int64_t s_row = row0 + row;
+    const int64_t s_row = row0 + x * kTileM + row;
     const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
     uint4* orow = reinterpret_cast<uint4*>(out + (b * nq + dst) * kD);
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float o[32];
       if (have) {
-        tmem_ld32(tmem + lane_base + 256 + cb * 32, o);
+        tmem_ld32(tO + cb * 32, o);
       } else {
 #pragma unroll
-        for (int x = 0; x < 32; ++x) o[x] = 0.f;
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
       if (row < rows) {
 #pragma unroll
@@ -338,8 +422,8 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
-            w[e] = *reinterpret_cast<uint32_t*>(&h);
+            __nv_bfloat162 hh = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
+            w[e] = *reinterpret_cast<uint32_t*>(&hh);
           }
           orow[cb * 4 + q4] = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -348,7 +432,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc<512>(tmem);
   }
@@ -384,8 +468,8 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
   int s = check_launch("attention tile table");
   if (s) return s;
   cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-  // Upper bound on tiles per problem: every cluster may add one partial tile.
-  const int64_t max_tiles = (nq + kTileM - 1) / kTileM + cq;
+  // Upper bound on 256-row units per problem: every cluster may add one partial unit.
+  const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
   dim3 grid((unsigned)max_tiles, (unsigned)bh);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
   block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
@@ -463,7 +547,7 @@ extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_p
   tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   if ((s = check_launch("attention tile table"))) return s;
   cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-  const int64_t max_tiles = (nq + kTileM - 1) / kTileM + cq;
+  const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
   dim3 grid((unsigned)max_tiles, (unsigned)bh);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
   block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
