@@ -133,6 +133,7 @@ def run_b200(args):
     from sparsepr_b200 import N8V6Config, N8V6Core, kernels as K, sparse_attention
     from sparsepr_b200.attention import kept_flops
     from sparsepr_b200.graph import GraphedSparseAttention, StreamedSparseAttention
+    from sparsepr_b200.sharding import head_shard, reduce_step_stats
     from sparsepr_b200.synthetic import synthetic_qkv
 
     world, rank, local = _dist()
@@ -144,9 +145,11 @@ def run_b200(args):
     if args.heads:
         cfgd["heads"] = args.heads
     heads = cfgd["heads"]
-    if heads % world:
-        raise SystemExit(f"{heads} heads do not shard over {world} GPUs")
-    local_heads = heads // world
+    try:
+        h0, h1 = head_shard(heads, world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
+    local_heads = h1 - h0
     grid = cfgd["grid"]
     n = grid[0] * grid[1] * grid[2]
     # Synthetic Q/K/V for this rank's heads, generated on the device (seeded per rank).
@@ -232,14 +235,8 @@ def run_b200(args):
     h2d = 3 * hq.numel() * 2
     d2h = hout.numel() * 2
 
-    stats = torch.tensor([ms, e2e_ms, attn_ms, kept, attn_flops], dtype=torch.float64, device=dev)
+    (ms, e2e_ms, attn_ms), (kept, attn_flops) = reduce_step_stats([ms, e2e_ms, attn_ms], [kept, attn_flops], dev)
     if world > 1:
-        mx = stats.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = stats.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms, e2e_ms, attn_ms = mx[0].item(), mx[1].item(), mx[2].item()
-        kept, attn_flops = sm[3].item(), sm[4].item()
         h2d *= world
         d2h *= world
     if rank == 0:
