@@ -362,26 +362,33 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       }
       const unsigned long long sc2 = pk2(scale_log2, scale_log2), nm2 = pk2(-m_run, -m_run);
       unsigned long long sum2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial sums (+0.0f pairs)
-      uint32_t pk[kTileN / 2];
+      // P(j) over the first 64 columns of S(j) (already loaded above), in two
+      // 64-key halves stored as soon as each is packed.
 #pragma unroll
-      for (int i = 0; i < kTileN; i += 2) {
-        float x0, x1, p0, p1;
-        up2(fma2(pk2(s[i], s[i + 1]), sc2, nm2), x0, x1);
-        if ((i & 7) == 0) {  // one pair in four on the FMA pipe, the rest on MUFU
-          ex2_fma2(x0, x1, p0, p1);
-        } else {
-          p0 = ex2(x0);
-          p1 = ex2(x1);
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[kTileN / 4];
+#pragma unroll
+        for (int i = 64 * hf; i < 64 * hf + 64; i += 2) {
+          float x0, x1, p0, p1;
+          up2(fma2(pk2(s[i], s[i + 1]), sc2, nm2), x0, x1);
+          if ((i & 7) == 0) {  // one pair in four on the FMA pipe, the rest on MUFU
+            ex2_fma2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          sum2[(i >> 1) & 3] = add2(sum2[(i >> 1) & 3], pk2(p0, p1));
+          __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
+          pk[(i - 64 * hf) >> 1] = *reinterpret_cast<uint32_t*>(&hh);
         }
-        sum2[(i >> 1) & 3] = add2(sum2[(i >> 1) & 3], pk2(p0, p1));
-        __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
-        pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
+        tmem_st32(tS + 32 * hf, reinterpret_cast<const float*>(pk));
       }
       float a0, a1, b0, b1;
       up2(add2(sum2[0], sum2[1]), a0, a1);
       up2(add2(sum2[2], sum2[3]), b0, b1);
       l_run = l_run * alpha + ((a0 + a1) + (b0 + b1));
-      // PV_x(j-1) is complete (S_x(j) completed after it): O_x may be rescaled.
+      // PV_x(j-1) is complete (S_x(j) completed after it): O_x may be rescaled
+      // (PV_x(j) waits for the arrive below).
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // warp-uniform: TMEM ld/st are warp-collective
         float o[32];
 #pragma unroll
@@ -392,9 +399,6 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           tmem_st32(tO + cb * 32, o);
         }
       }
-      // P(j) over the first 64 columns of S(j) (already loaded above).
-      tmem_st32(tS, reinterpret_cast<const float*>(pk));
-      tmem_st32(tS + 32, reinterpret_cast<const float*>(pk + 32));
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full[x]);
