@@ -128,8 +128,30 @@ sym_eig_kernel(const float* __restrict__ a_in, float* __restrict__ evals, float*
 // J_a^T A_ab J_b, so each thread rotates whole 2x2 blocks (both sides at
 // once; diagonal blocks get their exact zero off-diagonal) and the V columns
 // of its pairs in the same phase.  Rotation parameters are packed as one
-// float4 {c, s, p, q} per pair.  1024 threads, two barriers per round.
+// float4 {c, s, p, q} per pair.  1024 threads, two barriers per round.  V is
+// held in registers (see below), so a round moves only A through shared memory.
 constexpr int kEigBigThreads = 1024;
+
+// Packed fp32 pairs (sm_100 f32x2 instructions).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 
 template <int N>
 __global__ void __launch_bounds__(kEigBigThreads, 1)
@@ -137,12 +159,15 @@ sym_eig_big_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
                    int max_sweeps, float rel_tol) {
   constexpr int n = N, half = N / 2, ld = N + 1;
   constexpr int kBlocks = half * half / kEigBigThreads;  // 2x2 blocks per thread
-  constexpr int kVItems = n * half / kEigBigThreads;     // (row, pair) V updates per thread
-  static_assert(kBlocks >= 1 && kVItems >= 1, "size not supported");
+  // V lives in registers: thread = (row, run of kPPL consecutive pairs).
+  constexpr int kLanesPerRow = kEigBigThreads / n;  // 8 (n = 128) or 16 (n = 64): one row per lane group
+  constexpr int kPPL = half / kLanesPerRow;         // pairs per thread
+  static_assert(kBlocks >= 1 && kPPL >= 2 && 32 % kLanesPerRow == 0, "size not supported");
   extern __shared__ float sh[];
   float* A = sh;            // [n][ld]
-  float* V = sh + n * ld;   // [n][ld]
-  __shared__ float4 s_rot[half];
+  // Rotation of pair t at s_rot[t + t/8]: the padding keeps the eight lanes of a
+  // row group (reading pairs t0..t0+7, t0 = 8 x lane) on different banks.
+  __shared__ float4 s_rot[half + half / 8];
   __shared__ int s_rank[N];
   __shared__ float s_red[kEigBigThreads / 32][2];
   __shared__ int s_stop;
@@ -152,7 +177,16 @@ sym_eig_big_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
   for (int idx = tid; idx < n * n; idx += kEigBigThreads) {
     const int i = idx / n, j = idx % n;
     A[i * ld + j] = 0.5f * (src[i * n + j] + src[j * n + i]);
-    V[i * ld + j] = i == j ? 1.f : 0.f;
+  }
+  // Pair t of a round holds the matrix indices at circle positions t and
+  // n-1-t; vf/vs are this row's V entries at those two positions.  Round 0
+  // has position i = index i, and a full sweep (n-1 rounds) returns there.
+  const int vrow = tid / kLanesPerRow, t0 = (tid % kLanesPerRow) * kPPL;
+  float vf[kPPL], vs[kPPL];
+#pragma unroll
+  for (int u = 0; u < kPPL; ++u) {
+    vf[u] = vrow == t0 + u ? 1.f : 0.f;
+    vs[u] = vrow == n - 1 - (t0 + u) ? 1.f : 0.f;
   }
   __syncthreads();
   for (int sweep = 0; sweep < max_sweeps; ++sweep) {
@@ -182,48 +216,77 @@ sym_eig_big_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
         // Round-robin schedule: slot 0 holds index 0, slot i >= 1 holds
         // 1 + (i - 1 + round) mod (n - 1); pair t is (slot t, slot n-1-t).
         auto slot = [&](int i) { return i == 0 ? 0 : 1 + (i - 1 + round) % (n - 1); };
-        int p = slot(tid), q = slot(n - 1 - tid);
-        if (p > q) { const int t = p; p = q; q = t; }
+        const int f = slot(tid), g = slot(n - 1 - tid);
+        const int p = min(f, g), q = max(f, g);
         const float apq = A[p * ld + q];
         float c = 1.f, s = 0.f;
         if (fabsf(apq) > 1e-30f) {
-          const float tau = (A[q * ld + q] - A[p * ld + p]) / (2.f * apq);
-          const float t = copysignf(1.f, tau) / (fabsf(tau) + sqrtf(1.f + tau * tau));
+          // Approximate divisions shorten the serial step of the round: the
+          // angle only steers convergence, and c, s below stay a consistent
+          // rotation (c^2 + s^2 = 1 to rounding) whatever t is.
+          const float tau = __fdividef(A[q * ld + q] - A[p * ld + p], 2.f * apq);
+          const float t = __fdividef(copysignf(1.f, tau), fabsf(tau) + sqrtf(fmaf(tau, tau, 1.f)));
           c = rsqrtf(1.f + t * t);
           s = t * c;
         }
-        s_rot[tid] = make_float4(c, s, __int_as_float(p), __int_as_float(q));
+        // Oriented by circle position: with (first, second) = (f, g) the
+        // rotation reads row f <- c row f - s' row g, row g <- s' row f + c row g
+        // where s' = s when f is the smaller index and -s otherwise.
+        s_rot[tid + (tid >> 3)] = make_float4(c, f == p ? s : -s, __int_as_float(f), __int_as_float(g));
       }
       __syncthreads();
 #pragma unroll
       for (int k = 0; k < kBlocks; ++k) {
         const int z = tid + k * kEigBigThreads;
         const int ia = z / half, ib = z % half;
-        const float4 ra = s_rot[ia], rb = s_rot[ib];
+        const float4 ra = s_rot[ia + (ia >> 3)], rb = s_rot[ib + (ib >> 3)];
         const int pa = __float_as_int(ra.z), qa = __float_as_int(ra.w);
         const int pb = __float_as_int(rb.z), qb = __float_as_int(rb.w);
         const float x00 = A[pa * ld + pb], x01 = A[pa * ld + qb], x10 = A[qa * ld + pb], x11 = A[qa * ld + qb];
-        // Rows (J_a^T): row p <- c row p - s row q, row q <- s row p + c row q.
-        const float y00 = ra.x * x00 - ra.y * x10, y01 = ra.x * x01 - ra.y * x11;
-        const float y10 = ra.y * x00 + ra.x * x10, y11 = ra.y * x01 + ra.x * x11;
-        // Columns (J_b): the same on columns p, q.
-        float z00 = rb.x * y00 - rb.y * y01, z01 = rb.y * y00 + rb.x * y01;
-        float z10 = rb.x * y10 - rb.y * y11, z11 = rb.y * y10 + rb.x * y11;
+        // Rows (J_a^T): row p <- c row p - s row q, row q <- s row p + c row q,
+        // as packed pairs over the block's two columns.
+        const unsigned long long r0 = pk2(x00, x01), r1 = pk2(x10, x11);
+        const unsigned long long ca = pk2(ra.x, ra.x), sa = pk2(ra.y, ra.y), nsa = pk2(-ra.y, -ra.y);
+        float y00, y01, y10, y11;
+        up2(fma2(ca, r0, mul2(nsa, r1)), y00, y01);
+        up2(fma2(sa, r0, mul2(ca, r1)), y10, y11);
+        // Columns (J_b): the same on columns p, q, packed over each row's pair.
+        const unsigned long long cb2 = pk2(rb.x, rb.y), sb2 = pk2(-rb.y, rb.x);  // [c, s], [-s, c]
+        float z00, z01, z10, z11;
+        up2(fma2(pk2(y00, y00), cb2, mul2(pk2(y01, y01), sb2)), z00, z01);
+        up2(fma2(pk2(y10, y10), cb2, mul2(pk2(y11, y11), sb2)), z10, z11);
         if (ia == ib) z01 = z10 = 0.f;  // the rotated pair's own off-diagonal
         A[pa * ld + pb] = z00;
         A[pa * ld + qb] = z01;
         A[qa * ld + pb] = z10;
         A[qa * ld + qb] = z11;
       }
+      // V <- V J on this row's pairs (registers), then advance the circle:
+      // every position except 0 takes the content of the next position
+      // (position i+1 -> i, position 1 -> n-1), a neighbour exchange between
+      // consecutive pairs: within the thread or one shuffle away.
 #pragma unroll
-      for (int k = 0; k < kVItems; ++k) {
-        const int z = tid + k * kEigBigThreads;
-        const int i = z / half, ib = z % half;
-        const float4 rb = s_rot[ib];
-        const int pb = __float_as_int(rb.z), qb = __float_as_int(rb.w);
-        const float vp = V[i * ld + pb], vq = V[i * ld + qb];
-        V[i * ld + pb] = rb.x * vp - rb.y * vq;
-        V[i * ld + qb] = rb.y * vp + rb.x * vq;
+      for (int u = 0; u < kPPL; ++u) {
+        const int t = t0 + u;
+        const float4 r = s_rot[t + (t >> 3)];  // oriented: first = position t
+        // [first, second] <- first * [c, s] + second * [-s, c]
+        up2(fma2(pk2(vf[u], vf[u]), pk2(r.x, r.y), mul2(pk2(vs[u], vs[u]), pk2(-r.y, r.x))), vf[u], vs[u]);
+      }
+      {
+        const float next_first = __shfl_down_sync(0xffffffffu, vf[0], 1);
+        const float prev_second = __shfl_up_sync(0xffffffffu, vs[kPPL - 1], 1);
+        float nf[kPPL], ns[kPPL];
+#pragma unroll
+        for (int u = 0; u < kPPL; ++u) {
+          const int t = t0 + u;
+          nf[u] = t == 0 ? vf[0] : (t == half - 1 ? vs[u] : (u + 1 < kPPL ? vf[u + 1] : next_first));
+          ns[u] = t == 0 ? vf[1] : (u > 0 ? vs[u - 1] : prev_second);
+        }
+#pragma unroll
+        for (int u = 0; u < kPPL; ++u) {
+          vf[u] = nf[u];
+          vs[u] = ns[u];
+        }
       }
       __syncthreads();
     }
@@ -239,10 +302,12 @@ sym_eig_big_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
     s_rank[j] = rank;
   }
   __syncthreads();
+  // Whole sweeps only, so positions are back to indices: pair t = (t, n-1-t).
   float* out = evecs + b * (int64_t)n * n;
-  for (int idx = tid; idx < n * n; idx += kEigBigThreads) {
-    const int i = idx / n, j = idx % n;
-    out[i * n + s_rank[j]] = V[i * ld + j];
+#pragma unroll
+  for (int u = 0; u < kPPL; ++u) {
+    out[vrow * n + s_rank[t0 + u]] = vf[u];
+    out[vrow * n + s_rank[n - 1 - (t0 + u)]] = vs[u];
   }
 }
 
@@ -263,7 +328,7 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
   const int smem = 2 * kEigMax * kEigLd * (int)sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
   if (n == 64 || n == 128) {
-    const int big = 2 * n * (n + 1) * (int)sizeof(float);
+    const int big = n * (n + 1) * (int)sizeof(float);
     auto kern = n == 64 ? sym_eig_big_kernel<64> : sym_eig_big_kernel<128>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
     kern<<<(unsigned)batch, kEigBigThreads, big, st>>>(a, evals, evecs, max_sweeps, tol);
