@@ -119,6 +119,22 @@ int spr_permute_rows(const void* x, const int32_t* idx, void* y, int64_t bh, int
 /* ---------------------------------------------------------------- routing */
 
 /*
+ * Wan producer step: full-channel RMSNorm of Q and K (mean of squares over all
+ * C = heads*head_dim channels of a token, fp32), times the norm weight, rounded
+ * to the model dtype; complex RoPE on channel pairs (2i, 2i+1) of each head
+ * with freq_real/freq_imag [tokens, head_dim/2] fp32; rounded again; written as
+ * [batch, heads, tokens, head_dim].  V is only re-laid out.  q, k, v
+ * [batch, tokens, C] and the weights [C] share `dtype` (SPR_BF16, SPR_F16 or
+ * SPR_F32); head_dim even and a multiple of 8 (16-bit) / 4 (fp32).
+ * Replaces wan_qkv_norm_rope_layout (src/sparsepr/kernels/n8_ext/csrc/n8_ops.cu:357-411,
+ * kernel 16-105; Python entry kernels/n8_extension.py).
+ */
+int spr_wan_qkv_norm_rope_layout(const void* q, const void* k, const void* v, const void* q_weight,
+                                 const void* k_weight, const float* freq_real, const float* freq_imag, int dtype,
+                                 int64_t batch, int64_t tokens, int channels, int heads, float epsilon, void* q_out,
+                                 void* k_out, void* v_out, void* stream);
+
+/*
  * Attention-mass selector scores: scores[b,q,c] = log sum_{t in cluster c}
  * exp(qc[b,q].k_sorted[b,t] / sqrt(d)), -inf for empty clusters.
  * q_centroids [bh,cq,d] fp32, k_sorted [bh,n,d] bf16, k_offsets [bh,ck+1] i32;

@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import torch
 
 __all__ = [
+    "wan_qkv_norm_rope_layout",
     "euclid_assign",
     "assign_margin",
     "centroid_update",
@@ -584,3 +585,32 @@ def oracle_sparse_attention(q, k, v, cfg, *, route=None, **route_kw):
     base = inverse_permute_rows(out_perm, route.q_order)
     out, state, rows, weights, dense = oracle_repair(base, q3, k3, v3, route, cfg)
     return out.view(b, h, n, d), route, base, (state, rows, weights, dense)
+
+
+def wan_qkv_norm_rope_layout(q, k, v, q_weight, k_weight, freq_real, freq_imag, heads: int, epsilon: float):
+    """CPU restatement of the reference's fused Wan producer kernel
+    (``src/sparsepr/kernels/n8_ext/csrc/n8_ops.cu:16-105``, host 357-411).
+
+    Per token row: mean of squares over all C channels in fp32, ``inv =
+    1/sqrt(mean + eps)``; ``x * inv * w`` in fp32 rounded once to the model
+    dtype (the kernel's order; Wan's torch path rounds before the weight);
+    RoPE on channel pairs (2i, 2i+1) of each head, ``(a + ib)(fr + i fi)`` in
+    fp32, rounded to the model dtype; layout [B,L,C] -> [B,H,L,D].  V is only
+    re-laid out.
+    """
+    b, l, c = q.shape
+    hd = c // heads
+    dt = q.dtype
+
+    def norm_rope(x, w):
+        xf = x.float()
+        inv = torch.rsqrt(xf.square().mean(dim=-1, keepdim=True) + epsilon)
+        y = (xf * inv * w.float()).to(dt).float().view(b, l, heads, hd // 2, 2)
+        a, bb = y[..., 0], y[..., 1]
+        fr = freq_real.float().view(1, l, 1, hd // 2)
+        fi = freq_imag.float().view(1, l, 1, hd // 2)
+        out = torch.stack((a * fr - bb * fi, a * fi + bb * fr), dim=-1).to(dt)
+        return out.view(b, l, heads, hd).permute(0, 2, 1, 3).contiguous()
+
+    vo = v.view(b, l, heads, hd).permute(0, 2, 1, 3).contiguous()
+    return norm_rope(q, q_weight), norm_rope(k, k_weight), vo

@@ -18,5 +18,6 @@ from .attention import (  # noqa: F401
     sparse_attention,
 )
 from .kmeans import FlashKMeans, batch_kmeans_Euclid  # noqa: F401
+from .kernels import wan_qkv_norm_rope_layout  # noqa: F401
 
 __version__ = "0.1.0"

@@ -128,14 +128,19 @@ def sparse_n8_attention_bhld(attn, q_bhld, k_bhld, v_bhld, seq_lens=None):
     return out.to(dtype), density, info
 
 
-def install_wan22_ti2v_sparse_patch(config: Wan22TI2VSparseConfig | None = None, module=None):
+def install_wan22_ti2v_sparse_patch(config: Wan22TI2VSparseConfig | None = None, module=None,
+                                    extension_module=None):
     """Install this build behind ``--attention sparsepr``.
 
     ``module`` is the reference adapter module (``sparsepr.adapters.wan22``);
     its ``_sparse_n8_attention_bhld`` is replaced by
     :func:`sparse_n8_attention_bhld` and its ``_make_n8_core`` by
     :func:`make_n8_core`, so the reference's Wan attention override routes
-    every sparse call through sparsepr_b200.  Returns the previous functions.
+    every sparse call through sparsepr_b200.  ``extension_module`` (optional,
+    ``sparsepr.kernels.n8_extension``) gets this build's
+    ``wan_qkv_norm_rope_layout``, which the adapter's fused Q/K/V producer path
+    (``SPARSEPR_N8_CUDA_EXT_WAN_QKV``) imports from there.  Returns the previous
+    attention and core functions.
     """
     global _CONFIG
     if config is not None:
@@ -147,4 +152,8 @@ def install_wan22_ti2v_sparse_patch(config: Wan22TI2VSparseConfig | None = None,
     previous = (getattr(module, "_sparse_n8_attention_bhld", None), getattr(module, "_make_n8_core", None))
     module._sparse_n8_attention_bhld = sparse_n8_attention_bhld
     module._make_n8_core = make_n8_core
+    if extension_module is not None:
+        from .kernels import wan_qkv_norm_rope_layout
+
+        extension_module.wan_qkv_norm_rope_layout = wan_qkv_norm_rope_layout
     return previous

@@ -310,3 +310,38 @@ def chol_solve(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     _count(1)
     _lib.call("spr_chol_solve", _p(a), _p(b), bt, m, b.shape[2], _p(x), _stream(dev))
     return x
+
+
+def wan_qkv_norm_rope_layout(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_weight: torch.Tensor,
+                             k_weight: torch.Tensor, freq_real: torch.Tensor, freq_imag: torch.Tensor, heads: int,
+                             epsilon: float):
+    """Wan RMSNorm + RoPE + [B,L,C] -> [B,H,L,D] layout for Q/K (V: layout only).
+
+    Same arguments and result as the reference's
+    ``sparsepr.kernels.n8_extension.wan_qkv_norm_rope_layout``
+    (``n8_ops.cu:357-411``): returns ``(q_out, k_out, v_out)``, each
+    ``[B, heads, L, C/heads]`` in the input dtype."""
+    dev = _cuda(q, k, v, q_weight, k_weight, freq_real, freq_imag)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _contig(name, t)
+    if q.shape != k.shape or q.shape != v.shape or q.dim() != 3:
+        raise RuntimeError(f"Wan QKV inputs must have matching [B,L,C] shapes, got {tuple(q.shape)}, "
+                           f"{tuple(k.shape)}, {tuple(v.shape)}")
+    if not (q.dtype == k.dtype == v.dtype == q_weight.dtype == k_weight.dtype) or q.dtype not in _DT:
+        raise RuntimeError("Wan QKV inputs and norm weights must share one of fp32/bf16/fp16")
+    if freq_real.dtype != torch.float32 or freq_imag.dtype != torch.float32:
+        raise RuntimeError("Wan RoPE frequency tensors must be FP32")
+    b, l, c = q.shape
+    if heads <= 0 or c % heads:
+        raise RuntimeError(f"Wan channels ({c}) must divide num_heads ({heads})")
+    hd = c // heads
+    if q_weight.numel() != c or k_weight.numel() != c:
+        raise RuntimeError("Wan norm weights must contain C elements")
+    if tuple(freq_real.shape) != (l, hd // 2) or tuple(freq_imag.shape) != (l, hd // 2):
+        raise RuntimeError(f"Wan RoPE frequencies must have shape [L,D/2] = [{l},{hd // 2}]")
+    outs = [torch.empty((b, heads, l, hd), dtype=q.dtype, device=dev) for _ in range(3)]
+    _count(1)
+    _lib.call("spr_wan_qkv_norm_rope_layout", _p(q), _p(k), _p(v), _p(q_weight.contiguous()),
+              _p(k_weight.contiguous()), _p(freq_real.contiguous()), _p(freq_imag.contiguous()), _DT[q.dtype], b, l,
+              c, heads, float(epsilon), _p(outs[0]), _p(outs[1]), _p(outs[2]), _stream(dev))
+    return tuple(outs)
