@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import torch
 
 __all__ = [
+    "svg_ear_value_error_scores",
     "wan_qkv_norm_rope_layout",
     "euclid_assign",
     "assign_margin",
@@ -614,3 +615,37 @@ def wan_qkv_norm_rope_layout(q, k, v, q_weight, k_weight, freq_real, freq_imag, 
 
     vo = v.view(b, l, heads, hd).permute(0, 2, 1, 3).contiguous()
     return norm_rope(q, q_weight), norm_rope(k, k_weight), vo
+
+
+def svg_ear_value_error_scores(qc, k_sorted, v_sorted, k_centroids, v_centroids, k_sizes):
+    """SVG-EAR value-error selector scores (``kernels/triton/svg_ear.py:95-193``,
+    wrapper 453-531, no Jensen term as the route calls it, ``n8_v6.py:984-998``).
+
+    For query centroid c and key cluster j with tokens t:
+        a = exp(q_c . kbar_j / sqrt(D)),  b_t = exp(q_c . k_t / sqrt(D))
+        score = log( (1/n_j) sum_t |a vbar_j - b_t v_t|^2 )
+    (-inf for an empty cluster; the error is floored at 1e-30 before the log),
+    evaluated here in float64 with a per-(c, j) max shift.
+    """
+    bh, cq, d = qc.shape
+    ck = k_centroids.shape[1]
+    off = cluster_offsets(k_sizes.long())
+    scale = 1.0 / math.sqrt(d)
+    out = torch.full((bh, cq, ck), float("-inf"), dtype=torch.float64)
+    for b in range(bh):
+        q = qc[b].double()
+        for j in range(ck):
+            s, e = int(off[b, j]), int(off[b, j + 1])
+            if e <= s:
+                continue
+            kt = k_sorted[b, s:e].double()
+            vt = v_sorted[b, s:e].double()
+            cl = (q @ k_centroids[b, j].double()) * scale              # [cq]
+            tl = (q @ kt.T) * scale                                     # [cq, nj]
+            m = torch.maximum(cl, tl.max(dim=1).values)
+            a = torch.exp(cl - m).unsqueeze(1)                          # [cq, 1]
+            bt = torch.exp(tl - m.unsqueeze(1))                         # [cq, nj]
+            vbar = v_centroids[b, j].double()
+            err = (a * a * vbar.dot(vbar) + bt * bt * (vt * vt).sum(1) - 2 * a * bt * (vt @ vbar)).clamp_min(0)
+            out[b, :, j] = torch.log((err.sum(1) / (e - s)).clamp_min(1e-30)) + 2 * m
+    return out.float()

@@ -109,3 +109,17 @@ def test_kmeans_loop_contract():
     assert it1 < 50
     assert torch.equal(l1, oracle.euclid_assign(x, c1))
     assert torch.equal(s1.sum(1), torch.full((2,), 300))
+
+
+def test_oracle_svg_ear_value_scores_match_reference_kernel():
+    """The oracle's value-error scores against the reference Triton kernel's own
+    outputs (run on CPU by Triton's interpreter, tests/golden/make_svg_golden.py)."""
+    cases = torch.load(os.path.join(os.path.dirname(__file__), "golden", "svg_ear_value_scores.pt"))
+    for c in cases:
+        got = oracle.svg_ear_value_error_scores(c["q_centroids"], c["k_sorted"], c["v_sorted"], c["k_centroids"],
+                                                c["v_centroids"], c["k_sizes"])
+        ref = c["scores"]
+        fin = torch.isfinite(ref)
+        assert torch.equal(fin, torch.isfinite(got))
+        assert (~fin).any()  # empty clusters score -inf
+        torch.testing.assert_close(got[fin], ref[fin], atol=1e-4, rtol=1e-5)
