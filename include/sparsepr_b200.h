@@ -145,6 +145,22 @@ int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, co
                               int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream);
 
 /*
+ * SVG-EAR value-error selector scores: for query centroid c and key cluster j
+ * with tokens t (sorted order), a = exp(qc.kbar_j/sqrt(d)), b_t = exp(qc.k_t/sqrt(d)),
+ *   scores[b,c,j] = log( (1/n_j) sum_t |a vbar_j - b_t v_t|^2 ),
+ * -inf for an empty cluster.  k_sorted, v_sorted [bh,n,d] bf16; q_centroids
+ * [bh,cq,d], k_centroids, v_centroids [bh,ck,d] fp32; d = 128.  Workspace from
+ * spr_svg_ear_value_scores_workspace_bytes.
+ * Replaces svg_ear_value_error_scores_triton (src/sparsepr/kernels/triton/svg_ear.py:453-531,
+ * kernel 95-193) as the route calls it (no Jensen term, n8_v6.py:984-998).
+ */
+size_t spr_svg_ear_value_scores_workspace_bytes(int64_t bh, int cq, int ck, int64_t n);
+int spr_svg_ear_value_scores(const float* q_centroids, const void* k_sorted, const void* v_sorted,
+                             const float* k_centroids, const float* v_centroids, const int32_t* k_offsets, int64_t bh,
+                             int cq, int ck, int64_t n, int d, float* scores, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
  * Status of the last spr_attention_mass_scores launch (synchronous copy):
  * *out = 0, or the code of a device-side bounded wait that gave up.
  */

@@ -512,8 +512,8 @@ def random_init_indices(bh: int, n: int, k: int, seed: int) -> torch.Tensor:
 def oracle_route(q, k, v, cfg, *, k_init=None, q_init=None, init_seed: int = 0,
                  tol: float = 0.0) -> OracleRoute:
     """Cold-start ``N8V6Core.route`` (``models/common/n8_v6.py:521-1172``) for
-    the attention-mass selector, fixed-density or top-p budgets, no GQA, no
-    text suffix.  ``cfg`` carries the ``N8V6Config`` fields used here.
+    the attention-mass or SVG-EAR value-error selector (``n8_v6.py:971-998``),
+    fixed-density or top-p budgets, no GQA, no text suffix.  ``cfg`` carries the ``N8V6Config`` fields used here.
     ``k_init``/``q_init`` are role-feature-space initial centroids; when
     omitted they are the rows at ``random_init_indices``."""
     b, h, n, d = q.shape
@@ -541,7 +541,10 @@ def oracle_route(q, k, v, cfg, *, k_init=None, q_init=None, init_seed: int = 0,
     q_order = stable_label_order(q_labels)
     k_perm = permute_rows(kf3, k_order)
     v_perm = permute_rows(vf3, k_order)
-    scores = attention_mass_scores(q_cent, k_perm, k_sizes)
+    if getattr(cfg, "selector_policy", "attention_mass") == "svg_ear_value":
+        scores = svg_ear_value_error_scores(q_cent, k_perm, v_perm, k_cent, v_cent, k_sizes)
+    else:
+        scores = attention_mass_scores(q_cent, k_perm, k_sizes)
     if cfg.selector_budget_mode == "fixed_density":
         budget = fixed_density_budget(cfg.target_density, cfg.probe_rows, n, n, 0)
         budgets = torch.full((bh, cfg.num_q_centroids), budget, dtype=torch.long)

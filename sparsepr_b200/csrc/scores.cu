@@ -87,14 +87,92 @@ __device__ void stage_centroid_row(const float* __restrict__ qrow, bool valid, u
   }
 }
 
+// Per-cluster and per-token terms of the SVG-EAR value-error score (VALUE
+// mode of scores_tc_kernel).
+// Per key cluster j (one warp): |vbar_j|^2, and for each token t of the
+// cluster (sorted order) |v_t|^2 and v_t . vbar_j.
+__global__ void value_terms_kernel(const __nv_bfloat16* __restrict__ vs, const float* __restrict__ vbar,
+                                   const int32_t* __restrict__ koff, int ck, int64_t n, int64_t total,
+                                   float* __restrict__ vc2, float* __restrict__ vn2, float* __restrict__ vu) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= total) return;
+  const int64_t b = w / ck;
+  const int j = (int)(w % ck);
+  const float4 cb = reinterpret_cast<const float4*>(vbar + (b * ck + j) * kSD)[lane];
+  float c2 = cb.x * cb.x + cb.y * cb.y + cb.z * cb.z + cb.w * cb.w;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c2 += __shfl_xor_sync(0xffffffffu, c2, o);
+  if (lane == 0) vc2[b * ck + j] = c2;
+  const int32_t beg = koff[b * (ck + 1) + j], end = koff[b * (ck + 1) + j + 1];
+  for (int32_t t = beg; t < end; ++t) {
+    const uint2 u = reinterpret_cast<const uint2*>(vs + (b * n + t) * kSD)[lane];
+    const __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    const __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    const float x0 = __low2float(h0), x1 = __high2float(h0), x2 = __low2float(h1), x3 = __high2float(h1);
+    float nn = x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3;
+    float dd = x0 * cb.x + x1 * cb.y + x2 * cb.z + x3 * cb.w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      nn += __shfl_xor_sync(0xffffffffu, nn, o);
+      dd += __shfl_xor_sync(0xffffffffu, dd, o);
+    }
+    if (lane == 0) {
+      vn2[b * n + t] = nn;
+      vu[b * n + t] = dd;
+    }
+  }
+}
+
+// clog[b][c][j] = q_c . kbar_j / sqrt(D): grid (ceil(ck/32), bh); the block
+// stages 32 centroid rows and each thread takes query centroids c.
+__global__ void __launch_bounds__(256) centroid_logits_kernel(const float* __restrict__ qc,
+                                                              const float* __restrict__ kbar, int cq, int ck,
+                                                              float* __restrict__ clog) {
+  __shared__ float4 s_k[32][kSD / 4];
+  const int64_t b = blockIdx.y;
+  const int j0 = blockIdx.x * 32;
+  for (int i = threadIdx.x; i < 32 * (kSD / 4); i += blockDim.x) {
+    const int jj = i / (kSD / 4), d4 = i % (kSD / 4);
+    s_k[jj][d4] = j0 + jj < ck ? reinterpret_cast<const float4*>(kbar + (b * ck + j0 + jj) * kSD)[d4]
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  const float scale = rsqrtf((float)kSD);
+  for (int c = threadIdx.x; c < cq; c += blockDim.x) {
+    const float4* qr = reinterpret_cast<const float4*>(qc + (b * cq + c) * kSD);
+    float acc[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) acc[jj] = 0.f;
+    for (int d4 = 0; d4 < kSD / 4; ++d4) {
+      const float4 qv = __ldg(qr + d4);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const float4 kv = s_k[jj][d4];
+        acc[jj] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, acc[jj]))));
+      }
+    }
+    for (int jj = 0; jj < 32 && j0 + jj < ck; ++jj) clog[(b * cq + c) * ck + j0 + jj] = acc[jj] * scale;
+  }
+}
+
+struct ValueTerms {
+  const float* clog;  // [bh][cq][ck] centroid logits q_c . kbar_j / sqrt(D)
+  const float* vc2;   // [bh][ck] |vbar_j|^2
+  const float* vn2;   // [bh][n]  |v_t|^2 (sorted token order)
+  const float* vu;    // [bh][n]  v_t . vbar_(cluster of t)
+};
+
+template <bool VALUE>
 __global__ void __launch_bounds__(kSThreads, 1)
 scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, const float* __restrict__ qc,
                  const int32_t* __restrict__ koff, int cq, int ck, int64_t n, int64_t items,
-                 float* __restrict__ scores, int* __restrict__ err) {
+                 float* __restrict__ scores, int* __restrict__ err, ValueTerms vt) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_a_full, bar_a_empty, bar_b_full[kSStages], bar_b_empty[kSStages], bar_d_full[2],
       bar_d_free[2], bar_mma_done;
   __shared__ uint32_t s_tmem;
+  __shared__ __align__(16) float s_vt[VALUE ? 2 : 1][2][kSN];  // token terms per tile (VALUE mode)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sa = tc::smem_addr(smem);
   const uint32_t sb = sa + kSplits * kSTile;
@@ -230,6 +308,7 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, const float* __restri
         akey = key;
         ++na;
       }
+      if constexpr (!VALUE) {
       float* out = scores + (b * cq + (row_ok ? c : 0)) * (int64_t)ck;
       // Cluster walk state: current cluster j ends at token jend.
       int j = c0;
@@ -299,6 +378,91 @@ scores_tc_kernel(const __grid_constant__ CUtensorMap kmap, const float* __restri
         tc::tc_fence_before();
         tc::mbar_arrive(&bar_d_free[db]);
       }
+      } else {
+      float* out = scores + (b * cq + (row_ok ? c : 0)) * (int64_t)ck;
+      const float* clog_row = vt.clog + (b * cq + (row_ok ? c : 0)) * (int64_t)ck;
+      // Cluster walk: current cluster j spans tokens [jbeg, jend).  Base-2
+      // running max m starts at the centroid logit c2; ea = sum 2^(2(l-m)) |v|^2,
+      // eb = sum 2^(l-m) v.vbar (l = token logit in base 2).
+      int j = c0;
+      int32_t jbeg = t0, jend = t0;
+      float c2 = 0.f, m = 0.f, ea = 0.f, eb = 0.f;
+      auto advance = [&]() {
+        while (j < c1) {
+          jbeg = __ldg(koff + b * (ck + 1) + j);
+          jend = __ldg(koff + b * (ck + 1) + j + 1);
+          if (jend > jbeg) {
+            c2 = __ldg(clog_row + j) * 1.4426950408889634f;
+            m = c2;
+            ea = 0.f;
+            eb = 0.f;
+            return;
+          }
+          if (row_ok) out[j] = -INFINITY;
+          ++j;
+        }
+      };
+      advance();
+      for (int32_t tt = t0; tt < t1; tt += kSN, ++nt) {
+        const int db = (int)(nt & 1);
+        // Stage this tile's token terms (all four epilogue warps take part,
+        // also after a wait gave up, so the named barrier is never short).
+        {
+          const int64_t t = tt + r;
+          s_vt[nt & 1][0][r] = t < t1 ? __ldg(vt.vn2 + b * n + t) : 0.f;
+          s_vt[nt & 1][1][r] = t < t1 ? __ldg(vt.vu + b * n + t) : 0.f;
+          tc::named_bar(1, kSEpi);
+        }
+        ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[db], (uint32_t)((nt >> 1) & 1), err, 44));
+        tc::tc_fence_after();
+        if (ok) {
+#pragma unroll 1
+          for (int blk = 0; blk < kSN / 32; ++blk) {
+            const int32_t bt = tt + blk * 32;
+            if (bt >= t1) break;
+            float acc[32];
+            tc::tmem_ld32(tmem + lane_base + db * kSN + blk * 32, acc);
+            const float* wn = &s_vt[nt & 1][0][blk * 32];
+            const float* wu = &s_vt[nt & 1][1][blk * 32];
+            const int32_t be = min(bt + 32, t1);
+            int32_t pos = bt;
+            while (pos < be) {  // runs of one cluster inside this 32-token block (warp-uniform)
+              const int32_t re = min(jend, be);
+              const int a = pos - bt, e = re - bt;
+              float bm = -INFINITY;
+#pragma unroll
+              for (int q = 0; q < 32; ++q) bm = (q >= a && q < e) ? fmaxf(bm, acc[q]) : bm;
+              const float mn = fmaxf(m, bm * sc);
+              const float rs = tc::ex2(m - mn);
+              float A = ea * rs * rs, B = eb * rs;
+              const float nm = -mn;
+#pragma unroll
+              for (int q = 0; q < 32; ++q) {
+                if (q >= a && q < e) {
+                  const float w = tc::ex2(fmaf(acc[q], sc, nm));
+                  A = fmaf(w * w, wn[q], A);
+                  B = fmaf(w, wu[q], B);
+                }
+              }
+              ea = A;
+              eb = B;
+              m = mn;
+              pos = re;
+              if (pos == jend) {  // cluster j complete
+                const float cnt = (float)(jend - jbeg);
+                const float av = tc::ex2(c2 - m);
+                const float err2 = fmaf(cnt * av * av, __ldg(vt.vc2 + b * ck + j), fmaf(-2.f * av, eb, ea));
+                if (row_ok) out[j] = (__log2f(fmaxf(err2 / cnt, 1e-30f)) + 2.f * m) * ln2;
+                ++j;
+                advance();
+              }
+            }
+          }
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bar_d_free[db]);
+      }
+      }
     }
   }
   tc::tc_fence_before();
@@ -326,21 +490,26 @@ extern "C" int spr_attention_mass_scores_status(int* out) {
   return SPR_OK;
 }
 
-extern "C" int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets,
-                                         int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream) {
-  if (d != kSD) return fail(SPR_ERR_SHAPE, "attention-mass scores require d=128, got %d", d);
+namespace {
+
+int check_score_shapes(const float* q_centroids, const void* k_sorted, int64_t bh, int cq, int ck, int64_t n, int d,
+                       const char* what) {
+  if (d != kSD) return fail(SPR_ERR_SHAPE, "%s require d=128, got %d", what, d);
   if (bh <= 0 || cq <= 0 || ck <= 0 || n <= 0 || bh > 65535 || n > INT32_MAX)
-    return fail(SPR_ERR_SHAPE, "attention-mass scores: bad shape bh=%lld cq=%d ck=%d n=%lld", (long long)bh, cq, ck,
-                (long long)n);
+    return fail(SPR_ERR_SHAPE, "%s: bad shape bh=%lld cq=%d ck=%d n=%lld", what, (long long)bh, cq, ck, (long long)n);
   if (!aligned(q_centroids, 16) || !aligned(k_sorted, 16))
-    return fail(SPR_ERR_ALIGN, "attention-mass scores: 16-byte alignment required");
+    return fail(SPR_ERR_ALIGN, "%s: 16-byte alignment required", what);
+  return SPR_OK;
+}
+
+template <bool VALUE>
+int launch_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets, int64_t bh, int cq,
+                  int ck, int64_t n, float* scores, ValueTerms vt, cudaStream_t st, const char* what) {
   // Keys [bh][n][128] bf16: box 64 features (128 bytes) x 128 tokens.
   CUtensorMap kmap;
-  int s = encode_map_3d(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k_sorted, kSD, n, bh, 64, kSN,
-                        "attention-mass scores");
+  int s = encode_map_3d(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k_sorted, kSD, n, bh, 64, kSN, what);
   if (s) return s;
-  cudaStream_t st = (cudaStream_t)stream;
-  cudaFuncSetAttribute(scores_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmem);
+  cudaFuncSetAttribute(scores_tc_kernel<VALUE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmem);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -349,6 +518,60 @@ extern "C" int spr_attention_mass_scores(const float* q_centroids, const void* k
   int* err = nullptr;
   cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_scores_err);
   cudaMemsetAsync(err, 0, sizeof(int), st);
-  scores_tc_kernel<<<grid, kSThreads, kSSmem, st>>>(kmap, q_centroids, k_offsets, cq, ck, n, items, scores, err);
-  return check_launch("attention-mass scores (tcgen05)");
+  scores_tc_kernel<VALUE><<<grid, kSThreads, kSSmem, st>>>(kmap, q_centroids, k_offsets, cq, ck, n, items, scores,
+                                                           err, vt);
+  return check_launch(what);
+}
+
+struct ValueWs {
+  float *clog, *vc2, *vn2, *vu;
+};
+
+ValueWs carve_value_ws(Carver& c, int64_t bh, int cq, int ck, int64_t n) {
+  ValueWs w;
+  w.clog = c.take<float>((size_t)bh * cq * ck);
+  w.vc2 = c.take<float>((size_t)bh * ck);
+  w.vn2 = c.take<float>((size_t)bh * n);
+  w.vu = c.take<float>((size_t)bh * n);
+  return w;
+}
+
+}  // namespace
+
+extern "C" int spr_attention_mass_scores(const float* q_centroids, const void* k_sorted, const int32_t* k_offsets,
+                                         int64_t bh, int cq, int ck, int64_t n, int d, float* scores, void* stream) {
+  int s = check_score_shapes(q_centroids, k_sorted, bh, cq, ck, n, d, "attention-mass scores");
+  if (s) return s;
+  return launch_scores<false>(q_centroids, k_sorted, k_offsets, bh, cq, ck, n, scores, ValueTerms{},
+                              (cudaStream_t)stream, "attention-mass scores (tcgen05)");
+}
+
+extern "C" size_t spr_svg_ear_value_scores_workspace_bytes(int64_t bh, int cq, int ck, int64_t n) {
+  Carver c(nullptr, 0);
+  carve_value_ws(c, bh, cq, ck, n);
+  return c.off + 256;
+}
+
+extern "C" int spr_svg_ear_value_scores(const float* q_centroids, const void* k_sorted, const void* v_sorted,
+                                        const float* k_centroids, const float* v_centroids,
+                                        const int32_t* k_offsets, int64_t bh, int cq, int ck, int64_t n, int d,
+                                        float* scores, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_score_shapes(q_centroids, k_sorted, bh, cq, ck, n, d, "SVG-EAR value scores");
+  if (s) return s;
+  if (!aligned(v_sorted, 16) || !aligned(k_centroids, 16) || !aligned(v_centroids, 16))
+    return fail(SPR_ERR_ALIGN, "SVG-EAR value scores: 16-byte alignment required");
+  Carver c(workspace, workspace_bytes);
+  ValueWs w = carve_value_ws(c, bh, cq, ck, n);
+  if (!workspace || !c.ok())
+    return fail(SPR_ERR_WORKSPACE, "SVG-EAR value scores: workspace %zu < %zu", workspace_bytes, c.off);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t warps = bh * ck;
+  value_terms_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+      (const __nv_bfloat16*)v_sorted, v_centroids, k_offsets, ck, n, warps, w.vc2, w.vn2, w.vu);
+  if ((s = check_launch("SVG-EAR value terms"))) return s;
+  centroid_logits_kernel<<<dim3((unsigned)((ck + 31) / 32), (unsigned)bh), 256, 0, st>>>(q_centroids, k_centroids,
+                                                                                        cq, ck, w.clog);
+  if ((s = check_launch("SVG-EAR centroid logits"))) return s;
+  return launch_scores<true>(q_centroids, k_sorted, k_offsets, bh, cq, ck, n, scores,
+                             ValueTerms{w.clog, w.vc2, w.vn2, w.vu}, st, "SVG-EAR value scores (tcgen05)");
 }

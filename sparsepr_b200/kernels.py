@@ -198,6 +198,32 @@ def attention_mass_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, k_o
     return scores
 
 
+def svg_ear_value_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, v_sorted: torch.Tensor,
+                         k_centroids: torch.Tensor, v_centroids: torch.Tensor, k_offsets: torch.Tensor) -> torch.Tensor:
+    """SVG-EAR value-error selector scores -> fp32 [B,Cq,Ck] (-inf for empty key clusters)."""
+    dev = _cuda(q_centroids, k_sorted, v_sorted, k_centroids, v_centroids, k_offsets)
+    b, cq, d = q_centroids.shape
+    ck = k_offsets.shape[1] - 1
+    n = k_sorted.shape[1]
+    if k_sorted.dtype != torch.bfloat16 or v_sorted.dtype != torch.bfloat16:
+        raise RuntimeError("k_sorted and v_sorted must be bf16")
+    if v_sorted.shape != k_sorted.shape or tuple(k_centroids.shape) != (b, ck, d) or \
+            tuple(v_centroids.shape) != (b, ck, d):
+        raise RuntimeError(f"SVG-EAR shapes: k {tuple(k_sorted.shape)}, v {tuple(v_sorted.shape)}, "
+                           f"kc {tuple(k_centroids.shape)}, vc {tuple(v_centroids.shape)}, ck={ck}")
+    qc = q_centroids.float().contiguous()
+    kc = k_centroids.float().contiguous()
+    vc = v_centroids.float().contiguous()
+    scores = torch.empty((b, cq, ck), dtype=torch.float32, device=dev)
+    nbytes = _lib.query("spr_svg_ear_value_scores_workspace_bytes", b, cq, ck, n)
+    ws = workspace(dev, nbytes, "svg_ear")
+    _count(3)
+    _lib.call("spr_svg_ear_value_scores", _p(qc), _p(_contig("k_sorted", k_sorted)),
+              _p(_contig("v_sorted", v_sorted)), _p(kc), _p(vc), _p(_contig("k_offsets", k_offsets)), b, cq, ck, n,
+              d, _p(scores), _p(ws), ws.numel(), _stream(dev))
+    return scores
+
+
 def scores_error_code() -> int:
     """Status word of the last attention-mass scores launch (0 = ok; synchronises)."""
     import ctypes

@@ -437,8 +437,6 @@ class N8V6Core:
         cfg.validate(dim)
         if int(gqa_group_size) != 1:
             raise NotImplementedError("gqa_group_size > 1 is not implemented in sparsepr_b200.")
-        if cfg.selector_policy != "attention_mass":
-            raise NotImplementedError("sparsepr_b200 implements the attention_mass selector policy.")
         if cfg.role_v_weight != 0.0:
             raise NotImplementedError("role_v_weight > 0 is not implemented in sparsepr_b200.")
         bh = batch * heads
@@ -505,7 +503,10 @@ class N8V6Core:
         self.q_centroids = q_cent
 
         # Selector scores, budgets and the cluster-pair map (n8_v6.py:957-1112).
-        scores = K.attention_mass_scores(q_cent, k_perm, k_off)
+        if cfg.selector_policy == "svg_ear_value":  # n8_v6.py:984-998 (no Jensen term)
+            scores = K.svg_ear_value_scores(q_cent, k_perm, v_perm, k_cent, v_cent, k_off)
+        else:  # attention_mass, n8_v6.py:971-983
+            scores = K.attention_mass_scores(q_cent, k_perm, k_off)
         total_keys = int(total_key_tokens) if total_key_tokens is not None else tokens
         if total_keys < tokens or always_attended_keys < 0 or always_attended_keys > total_keys:
             raise ValueError(

@@ -148,6 +148,31 @@ def test_attention_mass_scores(cuda, bh, n, cq, ck, used, qscale):
     torch.testing.assert_close(got[fin], ref[fin], atol=2e-4, rtol=1e-5)
 
 
+def test_svg_ear_value_scores(cuda):
+    """Value-error scores against the oracle: on the fixture inputs pinned to the
+    reference kernel, and on a larger case with chunk and tile boundaries."""
+    import os
+
+    cases = torch.load(os.path.join(os.path.dirname(__file__), "golden", "svg_ear_value_scores.pt"))
+    g = torch.Generator().manual_seed(21)
+    bh, n, cq, ck = 2, 5000, 200, 300
+    lab = torch.randint(0, ck - 5, (bh, n), generator=g)
+    sizes = torch.zeros(bh, ck, dtype=torch.long).scatter_add_(1, lab, torch.ones_like(lab)).int()
+    cases.append(dict(q_centroids=torch.randn(bh, cq, 128, generator=g), k_sorted=torch.randn(bh, n, 128, generator=g).bfloat16(),
+                      v_sorted=torch.randn(bh, n, 128, generator=g).bfloat16(), k_centroids=torch.randn(bh, ck, 128, generator=g),
+                      v_centroids=torch.randn(bh, ck, 128, generator=g), k_sizes=sizes))
+    for c in cases:
+        ref = oracle.svg_ear_value_error_scores(c["q_centroids"], c["k_sorted"], c["v_sorted"], c["k_centroids"],
+                                                c["v_centroids"], c["k_sizes"])
+        off = oracle.cluster_offsets(c["k_sizes"].long()).to(torch.int32).to(cuda)
+        got = K.svg_ear_value_scores(c["q_centroids"].to(cuda), c["k_sorted"].to(cuda), c["v_sorted"].to(cuda),
+                                     c["k_centroids"].to(cuda), c["v_centroids"].to(cuda), off).cpu()
+        assert K.scores_error_code() == 0
+        fin = torch.isfinite(ref)
+        assert torch.equal(fin, torch.isfinite(got))
+        torch.testing.assert_close(got[fin], ref[fin], atol=2e-3, rtol=0)
+
+
 def test_selector_known_answer(cuda):
     """tests/test_n8_extension.py:79-103 of the reference, through the C ABI."""
     scores = torch.tensor([[[4.0, 3.0, 2.0, 1.0], [1.0, 4.0, 3.0, 2.0]]], device=cuda)
