@@ -243,6 +243,24 @@ int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* eva
  */
 int spr_chol_solve(const float* a, const float* b, int64_t batch, int m, int nrhs, float* x, void* stream);
 
+/*
+ * Cholesky-QR of x [batch][n][r] (n, r <= 128): columns normalised to unit
+ * length, G = X^T X + mean(diag G)*relative_ridge*I = L L^T, out = X L^{-T}.
+ * When G is not positive definite: out = the normalised X and failed[b] = 1.
+ * Replaces the cholesky_qr step of warm_subspace_metric_factor
+ * (src/sparsepr/models/cosmos3/operator_kmeans.py:332-364).
+ */
+int spr_cholesky_qr(const float* x, int64_t batch, int n, int r, float relative_ridge, float* out, int32_t* failed,
+                    void* stream);
+
+/*
+ * Batched lower Cholesky factor l [batch][m][m] of a + scale[b]*relative_ridge*I,
+ * falling back to scale[b]*fallback_ridge; when both fail, l = I and failed[b] = 1.
+ * Replaces cholesky_with_device_fallback (operator_kmeans.py:154-218).
+ */
+int spr_ridge_cholesky(const float* a, const float* scale, int64_t batch, int m, float relative_ridge,
+                       float fallback_ridge, float* l, int32_t* failed, void* stream);
+
 /* ---------------------------------------------------------------- repair */
 
 /*

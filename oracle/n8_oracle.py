@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import torch
 
 __all__ = [
+    "warm_subspace_metric_factor",
     "svg_ear_value_error_scores",
     "wan_qkv_norm_rope_layout",
     "euclid_assign",
@@ -652,3 +653,46 @@ def svg_ear_value_error_scores(qc, k_sorted, v_sorted, k_centroids, v_centroids,
             err = (a * a * vbar.dot(vbar) + bt * bt * (vt * vt).sum(1) - 2 * a * bt * (vt @ vbar)).clamp_min(0)
             out[b, :, j] = torch.log((err.sum(1) / (e - s)).clamp_min(1e-30)) + 2 * m
     return out.float()
+
+
+def warm_subspace_metric_factor(metric, previous, rank, *, power_iters=2, orthogonalization="each_cholesky_qr2",
+                                rayleigh_ridge=1e-4, cholesky_qr_ridge=1e-5):
+    """Warm role factor by subspace iteration with the Rayleigh-Cholesky Ritz
+    step, restating ``operator_kmeans.py:221-477`` (Cholesky-QR 332-364,
+    ridge fallback ``cholesky_with_device_fallback`` 154-218).  Returns
+    ``(factor, basis, recovered)``."""
+    m = metric.float()
+    basis = previous.float()
+    basis = basis / torch.linalg.vector_norm(basis, dim=1, keepdim=True).clamp_min(1e-12)
+    recovered = torch.zeros(m.shape[0], dtype=torch.bool)
+
+    def chol_qr(x, ridge):
+        xn = x / torch.linalg.vector_norm(x, dim=1, keepdim=True).clamp_min(1e-12)
+        g = torch.bmm(xn.transpose(1, 2), xn)
+        g = 0.5 * (g + g.transpose(1, 2))
+        jit = g.diagonal(dim1=1, dim2=2).mean(dim=1, keepdim=True).clamp_min(1e-12) * ridge
+        g = g + torch.diag_embed(jit.expand(-1, g.shape[-1]))
+        ch, info = torch.linalg.cholesky_ex(g)
+        bad = info != 0
+        ch = torch.where(bad[:, None, None], torch.eye(g.shape[-1]).expand_as(ch), ch)
+        return torch.linalg.solve_triangular(ch, xn.transpose(1, 2), upper=False).transpose(1, 2), bad
+
+    for it in range(power_iters):
+        basis, bad = chol_qr(torch.bmm(m, basis), cholesky_qr_ridge)
+        recovered |= bad
+        if orthogonalization == "each_cholesky_qr2" and it == power_iters - 1:
+            basis, bad = chol_qr(basis, max(cholesky_qr_ridge, 1e-5))
+            recovered |= bad
+    r = torch.bmm(basis.transpose(1, 2), torch.bmm(m, basis))
+    r = 0.5 * (r + r.transpose(1, 2))
+    norm = r.diagonal(dim1=1, dim2=2).mean(dim=1).clamp_min(1e-12)
+    eye = torch.eye(r.shape[-1]).expand_as(r)
+    prim, pinfo = torch.linalg.cholesky_ex(r + (norm * rayleigh_ridge)[:, None, None] * eye)
+    fb, finfo = torch.linalg.cholesky_ex(r + (norm * max(1e-2, rayleigh_ridge))[:, None, None] * eye)
+    use_p = (pinfo == 0)[:, None, None]
+    use_f = (~use_p) & (finfo == 0)[:, None, None]
+    chol = torch.where(use_p, prim, torch.where(use_f, fb, eye))
+    recovered |= finfo != 0
+    factor = torch.bmm(basis, chol) / torch.sqrt(norm)[:, None, None]
+    recovered |= ~torch.isfinite(factor).all(dim=(1, 2)) | ~torch.isfinite(basis).all(dim=(1, 2))
+    return factor, basis, recovered

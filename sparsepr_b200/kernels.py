@@ -371,3 +371,31 @@ def wan_qkv_norm_rope_layout(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, 
               _p(k_weight.contiguous()), _p(freq_real.contiguous()), _p(freq_imag.contiguous()), _DT[q.dtype], b, l,
               c, heads, float(epsilon), _p(outs[0]), _p(outs[1]), _p(outs[2]), _stream(dev))
     return tuple(outs)
+
+
+def cholesky_qr(x: torch.Tensor, relative_ridge: float):
+    """Cholesky-QR with column normalisation and a relative ridge (warm role
+    factors): x [B,n,r] fp32 -> (orthonormalised [B,n,r], failed bool [B])."""
+    dev = _cuda(x)
+    b, n, r = x.shape
+    xc = x.float().contiguous()
+    out = torch.empty_like(xc)
+    failed = torch.empty(b, dtype=torch.int32, device=dev)
+    _count(1)
+    _lib.call("spr_cholesky_qr", _p(xc), b, n, r, float(relative_ridge), _p(out), _p(failed), _stream(dev))
+    return out, failed.bool()
+
+
+def ridge_cholesky(a: torch.Tensor, scale: torch.Tensor, relative_ridge: float, fallback_ridge: float = 1e-2):
+    """Lower Cholesky factor of a + scale*ridge*I with the reference's fallback
+    ridge: a [B,m,m], scale [B] -> (L [B,m,m], failed bool [B])."""
+    dev = _cuda(a, scale)
+    b, m, _ = a.shape
+    ac = a.float().contiguous()
+    sc = scale.float().contiguous()
+    l = torch.empty_like(ac)
+    failed = torch.empty(b, dtype=torch.int32, device=dev)
+    _count(1)
+    _lib.call("spr_ridge_cholesky", _p(ac), _p(sc), b, m, float(relative_ridge), float(fallback_ridge), _p(l),
+              _p(failed), _stream(dev))
+    return l, failed.bool()

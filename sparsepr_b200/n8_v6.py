@@ -232,6 +232,54 @@ def metric_factor(metric: torch.Tensor, rank: int) -> torch.Tensor:
     return evecs * torch.sqrt(evals / norm).unsqueeze(1)
 
 
+def warm_subspace_metric_factor(metric: torch.Tensor, previous: torch.Tensor, rank: int, *, power_iters: int = 2,
+                                orthogonalization: str = "each_cholesky_qr2", ritz_mode: str = "rayleigh_cholesky",
+                                rayleigh_ridge: float = 1e-4, cholesky_qr_ridge: float = 1e-5):
+    """Warm top-``rank`` metric factor by subspace iteration from the previous
+    basis (``operator_kmeans.py:221-477``): ``power_iters`` applications of the
+    metric, each followed by Cholesky-QR (and a second, corrective one at the
+    end for ``each_cholesky_qr2``), then the Ritz step: ``B chol(B^T M B)/sqrt(mean
+    diag)`` (``rayleigh_cholesky``) or the reduced eigendecomposition (``full``).
+    Returns ``(factor, basis, recovered)``; ``recovered`` marks heads whose
+    Cholesky failed or whose result is not finite."""
+    if metric.ndim != 3 or metric.shape[1] != metric.shape[2]:
+        raise RuntimeError(f"Expected batched square metrics, got {tuple(metric.shape)}.")
+    expected = (metric.shape[0], metric.shape[1], rank)
+    if tuple(previous.shape) != expected:
+        raise RuntimeError(f"Previous factor shape mismatch: got {tuple(previous.shape)}, expected {expected}.")
+    if power_iters < 1:
+        raise RuntimeError(f"power_iters must be positive, got {power_iters}.")
+    if orthogonalization not in {"each_cholesky_qr", "each_cholesky_qr2"} or ritz_mode not in {"rayleigh_cholesky",
+                                                                                            "full"}:
+        raise NotImplementedError(
+            "sparsepr_b200 implements warm factors with each_cholesky_qr[2] orthogonalization and "
+            f"rayleigh_cholesky / full Ritz steps; got {orthogonalization!r}, {ritz_mode!r}.")
+    m = metric.float()
+    basis = previous.float()
+    basis = basis / torch.linalg.vector_norm(basis, dim=1, keepdim=True).clamp_min(1e-12)
+    recovered = torch.zeros(m.shape[0], dtype=torch.bool, device=m.device)
+    for it in range(power_iters):
+        basis, failed = K.cholesky_qr(torch.bmm(m, basis), cholesky_qr_ridge)
+        recovered |= failed
+        if orthogonalization == "each_cholesky_qr2" and it == power_iters - 1:
+            basis, failed = K.cholesky_qr(basis, max(float(cholesky_qr_ridge), 1e-5))
+            recovered |= failed
+    rayleigh = torch.bmm(basis.transpose(1, 2), torch.bmm(m, basis))
+    rayleigh = 0.5 * (rayleigh + rayleigh.transpose(1, 2))
+    if ritz_mode == "rayleigh_cholesky":
+        normalizer = rayleigh.diagonal(dim1=1, dim2=2).mean(dim=1).clamp_min(1e-12)
+        chol, failed = K.ridge_cholesky(rayleigh, normalizer, rayleigh_ridge, 1e-2)
+        recovered |= failed
+        factor = torch.bmm(basis, chol) / torch.sqrt(normalizer)[:, None, None]
+    else:
+        evals, rot = K.sym_eig(rayleigh)
+        evals = evals.clamp_min(0.0)
+        normalizer = evals.mean(dim=1, keepdim=True).clamp_min(1e-12)
+        factor = torch.bmm(basis, rot) * torch.sqrt(evals / normalizer).unsqueeze(1)
+    recovered |= ~torch.isfinite(factor).all(dim=(1, 2)) | ~torch.isfinite(basis).all(dim=(1, 2))
+    return factor, basis, recovered
+
+
 class _MatmulPrecision:
     def __init__(self, precision: str):
         self.precision = precision
@@ -383,8 +431,9 @@ class N8V6Core:
     Cross-step state (previous original-space centroids and repair state) is
     kept like the reference: a second call warm-starts both k-means runs from
     the projected previous centroids with ``kmeans_iter_step`` iterations.
-    Role factors are recomputed exactly (eigh) on every call; the reference's
-    warm subspace iteration (``operator_kmeans.py:221-477``) is not implemented.
+    Role factors are exact (eigh) on the first call and updated by the
+    reference's warm subspace iteration (``operator_kmeans.py:221-477``) on
+    later refreshes.
     """
 
     def __init__(self, config: N8V6Config, init_indices: tuple[torch.Tensor, torch.Tensor] | None = None):
@@ -400,12 +449,34 @@ class N8V6Core:
         self.v_centroids: torch.Tensor | None = None
         self.q_factor_current: torch.Tensor | None = None
         self.k_factor_current: torch.Tensor | None = None
+        # Warm subspace bases the next factor update starts from (n8_v6.py:381-383).
+        self.q_factor_state: torch.Tensor | None = None
+        self.k_factor_state: torch.Tensor | None = None
+        self.q_factor_recovery_mask: torch.Tensor | None = None
+        self.k_factor_recovery_mask: torch.Tensor | None = None
         self.repair_state_current = None
         self.repair_recovery_mask: torch.Tensor | None = None
         self.route_call_index = 0
         self.last_route_profile: dict = {}
         self.last_repair_profile: dict = {}
         self.diagnostic_callback = None
+
+    def _updated_factor(self, metric, previous, current, rank):
+        """Exact factor on the first update, warm subspace iteration afterwards;
+        a head whose warm solve fails keeps its previous factor and basis
+        (``n8_v6.py:478-519``).  Returns ``(factor, state, recovered)``."""
+        cfg = self.config
+        if previous is None:
+            factor = metric_factor(metric, rank)
+            return factor, factor, torch.zeros(metric.shape[0], dtype=torch.bool, device=metric.device)
+        if current is None:
+            raise RuntimeError("Warm role-factor state is missing its current factor.")
+        factor, state, recovered = warm_subspace_metric_factor(
+            metric, previous, rank, power_iters=cfg.factor_power_iters,
+            orthogonalization=cfg.factor_orthogonalization, ritz_mode=cfg.factor_ritz_mode,
+            rayleigh_ridge=cfg.factor_rayleigh_ridge, cholesky_qr_ridge=cfg.factor_cholesky_qr_ridge)
+        sel = recovered[:, None, None]
+        return torch.where(sel, current.float(), factor), torch.where(sel, previous.float(), state), recovered
 
     @property
     def initialized(self) -> bool:
@@ -448,8 +519,16 @@ class N8V6Core:
         warm = self.initialized
         iters = cfg.kmeans_iter_step if warm else cfg.kmeans_iter_init
 
-        # Key role factor and features: K F_k / rms (n8_v6.py:612-681).
-        k_factor = metric_factor(key_metric_from_queries(q, cfg.metric_sample_tokens), cfg.role_k_rank)
+        # Key role factor and features: K F_k / rms (n8_v6.py:612-681).  Factors
+        # are refreshed on the first call and every factor_refresh_every calls.
+        refresh = (self.q_factor_current is None or self.k_factor_current is None
+                   or self.route_call_index % cfg.factor_refresh_every == 0)
+        if refresh:
+            k_factor, self.k_factor_state, self.k_factor_recovery_mask = self._updated_factor(
+                key_metric_from_queries(q, cfg.metric_sample_tokens), self.k_factor_state, self.k_factor_current,
+                cfg.role_k_rank)
+        else:
+            k_factor = self.k_factor_current
         self.k_factor_current = k_factor
         with _MatmulPrecision(cfg.role_kv_matmul_precision):
             k_feat = torch.bmm(k.float(), k_factor)
@@ -485,7 +564,12 @@ class N8V6Core:
         self.k_centroids, self.v_centroids = k_cent, v_cent
 
         # Query role factor from the key-centroid metric, row-RMS features (n8_v6.py:744-806).
-        q_factor = metric_factor(query_metric_from_key_centroids(k_cent, k_sizes), cfg.role_q_rank)
+        if refresh:
+            q_factor, self.q_factor_state, self.q_factor_recovery_mask = self._updated_factor(
+                query_metric_from_key_centroids(k_cent, k_sizes), self.q_factor_state, self.q_factor_current,
+                cfg.role_q_rank)
+        else:
+            q_factor = self.q_factor_current
         self.q_factor_current = q_factor
         with _MatmulPrecision(cfg.role_kv_matmul_precision):
             q_feat = torch.bmm(q.float(), q_factor)

@@ -173,6 +173,34 @@ def test_svg_ear_value_scores(cuda):
         torch.testing.assert_close(got[fin], ref[fin], atol=2e-3, rtol=0)
 
 
+def test_warm_role_factor_matches_oracle(cuda):
+    """Warm subspace factor update (Cholesky-QR and ridge-Cholesky kernels) on the
+    inputs pinned to the reference, against the oracle."""
+    import os
+
+    from sparsepr_b200.n8_v6 import warm_subspace_metric_factor
+
+    cases = torch.load(os.path.join(os.path.dirname(__file__), "golden", "warm_factor.pt"))
+    for c in cases:
+        f, b, rec = warm_subspace_metric_factor(c["metric"].to(cuda), c["previous"].to(cuda), c["rank"])
+        fo, bo, reco = oracle.warm_subspace_metric_factor(c["metric"], c["previous"], c["rank"])
+        assert torch.equal(rec.cpu(), reco)
+        torch.testing.assert_close(b.cpu(), bo, atol=2e-4, rtol=1e-3)
+        torch.testing.assert_close(f.cpu(), fo, atol=2e-4, rtol=1e-3)
+
+
+def test_cholesky_kernels_report_failure(cuda):
+    bad = -torch.eye(8).expand(2, 8, 8).clone()  # negative definite: every attempt fails
+    l, failed = K.ridge_cholesky(bad.to(cuda), torch.ones(2, device=cuda), 1e-4)
+    assert failed.all() and torch.equal(l.cpu(), torch.eye(8).expand(2, 8, 8))
+    x = torch.randn(2, 16, 4)
+    x[1, :, 1] = x[1, :, 0]  # rank deficient: Cholesky-QR of the second problem fails
+    out, failed = K.cholesky_qr(x.to(cuda), 1e-12)
+    assert failed.tolist() == [False, True]
+    q = out[0].cpu()
+    torch.testing.assert_close(q.T @ q, torch.eye(4), atol=1e-4, rtol=0)
+
+
 def test_selector_known_answer(cuda):
     """tests/test_n8_extension.py:79-103 of the reference, through the C ABI."""
     scores = torch.tensor([[[4.0, 3.0, 2.0, 1.0], [1.0, 4.0, 3.0, 2.0]]], device=cuda)

@@ -123,3 +123,14 @@ def test_oracle_svg_ear_value_scores_match_reference_kernel():
         assert torch.equal(fin, torch.isfinite(got))
         assert (~fin).any()  # empty clusters score -inf
         torch.testing.assert_close(got[fin], ref[fin], atol=1e-4, rtol=1e-5)
+
+
+def test_oracle_warm_factor_matches_reference():
+    """The oracle's warm subspace factor against the reference's own
+    warm_subspace_metric_factor (tests/golden/make_warm_factor_golden.py)."""
+    cases = torch.load(os.path.join(os.path.dirname(__file__), "golden", "warm_factor.pt"))
+    for c in cases:
+        f, b, rec = oracle.warm_subspace_metric_factor(c["metric"], c["previous"], c["rank"])
+        assert torch.equal(rec, c["recovered"])
+        torch.testing.assert_close(b, c["basis"], atol=1e-5, rtol=1e-4)
+        torch.testing.assert_close(f, c["factor"], atol=1e-5, rtol=1e-4)
