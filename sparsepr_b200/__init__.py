@@ -12,6 +12,8 @@ Public API:
 from .n8_v6 import N8V6Config, N8V6Core, N8V6Route  # noqa: F401
 from .attention import (  # noqa: F401
     Wan22TI2VSparseConfig,
+    hunyuan_sparse_attention,
+    install_hunyuan_sparse_patch,
     install_wan22_ti2v_sparse_patch,
     kept_flops,
     make_n8_core,

@@ -15,7 +15,7 @@ import torch
 from . import kernels as K
 from .n8_v6 import N8V6Config, N8V6Core
 
-__all__ = ["sparse_attention", "Wan22TI2VSparseConfig", "install_wan22_ti2v_sparse_patch", "make_n8_core",
+__all__ = ["sparse_attention", "hunyuan_sparse_attention", "hunyuan_attend", "install_hunyuan_sparse_patch", "Wan22TI2VSparseConfig", "install_wan22_ti2v_sparse_patch", "make_n8_core",
            "kept_flops", "sparse_n8_attention_bhld"]
 
 
@@ -50,6 +50,94 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     info["base"] = base
     info["repair_state"] = core.repair_state_current
     return repaired, float(info["effective_video_density"]), info
+
+
+def hunyuan_attend(query, key, value, core: N8V6Core, *, video_tokens: int, prompt_length: int):
+    """Route and block-sparse attention of :func:`hunyuan_sparse_attention`
+    before the repair: returns ``(attended [1,H,N,D] in token order, route,
+    video queries)``.
+
+    ``query/key/value`` [1,H,video+text,D]: video tokens first, then the text
+    context (``prompt_length`` real prompt tokens, then padding).  Routing sees
+    the video tokens (prompt keys always attended, the full K/V as permute
+    source).  Two text clusters extend the map: every video query cluster
+    also attends the prompt; the prompt rows attend every video key cluster
+    and the prompt; padding rows attend only the padding.
+    """
+    if query.ndim != 4 or key.shape != query.shape or value.shape != query.shape:
+        raise RuntimeError(f"Hunyuan SparsePR expects matching [B,H,N,D] tensors, got {tuple(query.shape)}, "
+                           f"{tuple(key.shape)}, {tuple(value.shape)}.")
+    batch, heads, tokens, dim = query.shape
+    text = tokens - int(video_tokens)
+    if batch != 1 or text < 0 or not 0 <= prompt_length <= text:
+        raise RuntimeError(f"Hunyuan sequence mismatch: {tokens} tokens, video {video_tokens}, prompt {prompt_length}.")
+    dev = query.device
+    q_video = query[:, :, :video_tokens].contiguous()
+    k_video = key[:, :, :video_tokens].contiguous()
+    v_video = value[:, :, :video_tokens].contiguous()
+    route = core.route(q_video, k_video, v_video, always_attended_keys=int(prompt_length),
+                       total_key_tokens=int(video_tokens) + int(prompt_length), k_full_source=key,
+                       v_full_source=value)
+    if not route.permuted_includes_suffix:
+        raise RuntimeError("SparsePR did not return the full Hunyuan K/V layout.")
+    bh = batch * heads
+    cq, ck = route.selected_ids.shape[1], route.selected_ids.shape[2]
+    # Query order: video rows by cluster, text rows in place.
+    suffix = torch.arange(video_tokens, tokens, device=dev, dtype=torch.int32).expand(bh, -1)
+    q_order = torch.cat((route.q_sorted_indices.to(torch.int32), suffix), dim=1).contiguous()
+    q_perm = K.permute_rows(query.to(torch.bfloat16).contiguous().view(bh, tokens, dim), q_order)
+    # Cluster layout with the prompt and padding clusters appended to both sides.
+    tail = torch.tensor([video_tokens + prompt_length, tokens], device=dev, dtype=torch.int32).expand(bh, -1)
+    q_off = torch.cat((route.q_offsets.to(torch.int32), tail), dim=1).contiguous()
+    k_off = torch.cat((route.k_offsets.to(torch.int32), tail), dim=1).contiguous()
+    sel = torch.full((bh, cq + 2, ck + 2), -1, device=dev, dtype=torch.int32)
+    sel[:, :cq, :ck] = route.selected_ids
+    counts = torch.empty((bh, cq + 2), device=dev, dtype=torch.int32)
+    sel[:, :cq].scatter_(2, route.selected_counts.long().unsqueeze(-1), ck)  # + prompt cluster (highest id)
+    counts[:, :cq] = route.selected_counts + 1
+    sel[:, cq, :ck + 1] = torch.arange(ck + 1, device=dev, dtype=torch.int32)  # prompt rows: all but padding
+    counts[:, cq] = ck + 1
+    sel[:, cq + 1, 0] = ck + 1  # padding rows: padding only
+    counts[:, cq + 1] = 1
+    out = K.block_sparse_attention(q_perm, route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim),
+                                   q_off, k_off, sel, counts, q_order=q_order).view(batch, heads, tokens, dim)
+    return out, route, q_video
+
+
+def hunyuan_sparse_attention(query, key, value, core: N8V6Core, *, video_tokens: int, prompt_length: int):
+    """SparsePR call of the HunyuanVideo processor (``hunyuanvideo.py:160-239``).
+
+    ``query/key/value`` [1,H,video+text,D]: video tokens first, then the text
+    context (``prompt_length`` real prompt tokens, then padding).  Routing sees
+    the video tokens (prompt keys always attended, the full K/V as permute
+    source).  Two text clusters extend the map: every video query cluster
+    also attends the prompt; the prompt rows attend every video key cluster
+    and the prompt; padding rows attend only the padding.  Video rows are
+    repaired against K/V over video + prompt; text rows are returned as
+    attended.  Returns ``[1,H,video+text,D]`` bf16.
+    """
+    out, route, q_video = hunyuan_attend(query, key, value, core, video_tokens=video_tokens,
+                                         prompt_length=prompt_length)
+    keep = int(video_tokens) + int(prompt_length)
+    repaired, _info = core.repair(out[:, :, :video_tokens], q_video, key[:, :, :keep], value[:, :, :keep], route)
+    return torch.cat((repaired, out[:, :, video_tokens:]), dim=2)
+
+
+def install_hunyuan_sparse_patch(processor_cls, core_attr: str = "n8"):
+    """Route ``processor_cls._sparse_attention`` (the reference's
+    ``HunyuanVideoN8Processor``, ``hunyuanvideo.py:160-239``) through
+    :func:`hunyuan_sparse_attention`.  The processor keeps its own core in
+    ``core_attr``; it must be a ``sparsepr_b200.N8V6Core``.  Returns the
+    previous method."""
+    previous = getattr(processor_cls, "_sparse_attention", None)
+
+    def _sparse_attention(self, query, key, value):
+        return hunyuan_sparse_attention(query, key, value, getattr(self, core_attr),
+                                        video_tokens=self.num_frame_patches * self.frame_size,
+                                        prompt_length=self.prompt_length)
+
+    processor_cls._sparse_attention = _sparse_attention
+    return previous
 
 
 def kept_flops(route, head_dim: int, probe_rows: int, tokens: int) -> torch.Tensor:

@@ -254,3 +254,42 @@ def test_streamed_host_layer_matches_all_heads_graph(cuda):
         _close(hout.view(6, -1, 128), ref.view(6, -1, 128))
         same = sum(torch.equal(hout[0, h], ref[0, h]) for h in range(6))
         assert same >= 3, same
+
+
+@pytest.mark.parametrize("prompt,pad", [(30, 18), (48, 0)])
+def test_hunyuan_layout_matches_oracle(cuda, prompt, pad):
+    """Hunyuan boundary (video + text context): attention over the extended
+    cluster map built as hunyuanvideo.py:195-217 does (prompt and padding
+    clusters appended), against the oracle on the build's own route; text rows
+    come back unrepaired, video rows repaired."""
+    from sparsepr_b200.attention import hunyuan_attend, hunyuan_sparse_attention
+
+    cfg = _cfg()
+    qv, kv, vv = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(3)
+    text = prompt + pad
+    q, k, v = (torch.cat((t, torch.randn(1, 2, text, 128, generator=g).bfloat16()), dim=2) for t in (qv, kv, vv))
+    n_video = qv.shape[2]
+    core = N8V6Core(cfg)
+    att, route, _ = hunyuan_attend(q.to(cuda), k.to(cuda), v.to(cuda), core, video_tokens=n_video,
+                                   prompt_length=prompt)
+    bh, cq, ck = 2, route.selected_ids.shape[1], route.selected_ids.shape[2]
+    mask = torch.zeros(bh, cq + 2, ck + 2, dtype=torch.bool)
+    mask[:, :cq, :ck] = route.video_dynamic_map.cpu().view(bh, cq, ck)
+    mask[:, :cq, ck] = True
+    mask[:, cq, :ck + 1] = True
+    mask[:, cq + 1, ck + 1] = True
+    qs = torch.cat((route.q_cluster_sizes.cpu().view(bh, cq).long(), torch.tensor([[prompt, pad]] * bh)), 1)
+    ks = torch.cat((route.k_cluster_sizes.cpu().view(bh, ck).long(), torch.tensor([[prompt, pad]] * bh)), 1)
+    order = torch.cat((route.q_sorted_indices.cpu().long(), torch.arange(n_video, n_video + text).expand(bh, -1)), 1)
+    q3 = q.view(bh, -1, 128)
+    qp = torch.gather(q3, 1, order.unsqueeze(-1).expand(-1, -1, 128))
+    ref_p = oracle.block_sparse_attention(qp, route.k_permuted.view(bh, -1, 128).cpu(),
+                                          route.v_permuted.view(bh, -1, 128).cpu(), mask, qs, ks)
+    ref = torch.empty_like(ref_p).scatter_(1, order.unsqueeze(-1).expand(-1, -1, 128), ref_p)
+    _close(att.view(bh, -1, 128).cpu(), ref)
+    out = hunyuan_sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg), video_tokens=n_video,
+                                   prompt_length=prompt).cpu()
+    assert out.shape == q.shape and torch.isfinite(out.float()).all()
+    assert torch.equal(out[:, :, n_video:], att.cpu()[:, :, n_video:])  # text rows: attended, not repaired
+    assert not torch.equal(out[:, :, :n_video], att.cpu()[:, :, :n_video])  # video rows: repaired

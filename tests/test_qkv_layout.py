@@ -86,3 +86,15 @@ def test_install_patch_replaces_the_reference_entry_points():
     assert adapter._sparse_n8_attention_bhld is A.sparse_n8_attention_bhld
     assert adapter._make_n8_core is A.make_n8_core
     assert ext.wan_qkv_norm_rope_layout is K.wan_qkv_norm_rope_layout
+
+
+def test_install_hunyuan_patch_replaces_the_processor_method():
+    from sparsepr_b200 import attention as A
+
+    class Processor:
+        def _sparse_attention(self, query, key, value):
+            return "reference"
+
+    old = Processor._sparse_attention
+    prev = A.install_hunyuan_sparse_patch(Processor)
+    assert prev is old and Processor._sparse_attention is not old
