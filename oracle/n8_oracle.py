@@ -510,27 +510,50 @@ def random_init_indices(bh: int, n: int, k: int, seed: int) -> torch.Tensor:
     return torch.randint(0, n, (bh, k), generator=g)
 
 
+def _per_query_head(t, b, kvh, g):
+    """Copy a per-KV-head tensor to each query head of its GQA group
+    (``repeat_interleave`` over heads, ``n8_v6.py:762-834``)."""
+    return t.reshape(b, kvh, *t.shape[1:]).repeat_interleave(g, dim=1).reshape(b * kvh * g, *t.shape[1:])
+
+
 def oracle_route(q, k, v, cfg, *, k_init=None, q_init=None, init_seed: int = 0,
-                 tol: float = 0.0) -> OracleRoute:
+                 tol: float = 0.0, gqa_group_size: int = 1) -> OracleRoute:
     """Cold-start ``N8V6Core.route`` (``models/common/n8_v6.py:521-1172``) for
     the attention-mass or SVG-EAR value-error selector (``n8_v6.py:971-998``),
-    fixed-density or top-p budgets, no GQA, no text suffix.  ``cfg`` carries the ``N8V6Config`` fields used here.
+    fixed-density or top-p budgets, no text suffix.  ``cfg`` carries the ``N8V6Config`` fields used here.
     ``k_init``/``q_init`` are role-feature-space initial centroids; when
-    omitted they are the rows at ``random_init_indices``."""
+    omitted they are the rows at ``random_init_indices``.
+
+    GQA (``gqa_group_size`` g > 1, ``n8_v6.py:549-567, 762-834, 936-971``):
+    K/V are clustered on the first query head of each group with the key
+    metric pooled over the group's g*N queries (g times the sample count,
+    ``operator_kmeans.py:570-606``); the Q factor, K labels, sizes and
+    centroids are then copied to every query head of the group, and each
+    query head permutes its own K/V by the group's order.  The returned
+    ``k_features`` stay per KV head."""
     b, h, n, d = q.shape
-    bh = b * h
+    g = int(gqa_group_size)
+    if g <= 0 or h % g:
+        raise ValueError(f"gqa_group_size must divide the query-head count; got H={h}, G={g}.")
+    bh, kvh = b * h, h // g
     qf3, kf3, vf3 = (t.reshape(bh, n, d) for t in (q, k, v))
-    k_factor = metric_factor(key_metric_from_queries(qf3, cfg.metric_sample_tokens), cfg.role_k_rank)
-    kfeat = torch.bmm(kf3.float(), k_factor)
+    kn3 = k[:, ::g].reshape(b * kvh, n, d)
+    vn3 = v[:, ::g].reshape(b * kvh, n, d)
+    k_factor = metric_factor(key_metric_from_queries(qf3.reshape(b * kvh, g * n, d), cfg.metric_sample_tokens * g),
+                             cfg.role_k_rank)
+    kfeat = torch.bmm(kn3.float(), k_factor)
     kscale = kfeat.square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(1e-8)
     kfeat = kfeat / kscale
     if k_init is None:
-        idx = random_init_indices(bh, n, cfg.num_k_centroids, init_seed)
+        idx = random_init_indices(b * kvh, n, cfg.num_k_centroids, init_seed)
         k_init = torch.gather(kfeat, 1, idx.unsqueeze(-1).expand(-1, -1, kfeat.shape[-1]))
     k_labels, _, k_sizes, k_it = batch_kmeans_euclid(kfeat, cfg.num_k_centroids, cfg.kmeans_iter_init, tol, k_init)
-    k_cent = original_centroids(kf3, k_labels, k_sizes)
-    v_cent = original_centroids(vf3, k_labels, k_sizes)
+    k_cent = original_centroids(kn3, k_labels, k_sizes)
+    v_cent = original_centroids(vn3, k_labels, k_sizes)
     q_factor = metric_factor(query_metric_from_key_centroids(k_cent, k_sizes), cfg.role_q_rank)
+    if g > 1:
+        q_factor, k_labels, k_sizes, k_cent, v_cent = (_per_query_head(t, b, kvh, g)
+                                                      for t in (q_factor, k_labels, k_sizes, k_cent, v_cent))
     qfeat = torch.bmm(qf3.float(), q_factor)
     qfeat = qfeat / qfeat.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)
     if q_init is None:
@@ -543,7 +566,11 @@ def oracle_route(q, k, v, cfg, *, k_init=None, q_init=None, init_seed: int = 0,
     k_perm = permute_rows(kf3, k_order)
     v_perm = permute_rows(vf3, k_order)
     if getattr(cfg, "selector_policy", "attention_mass") == "svg_ear_value":
-        scores = svg_ear_value_error_scores(q_cent, k_perm, v_perm, k_cent, v_cent, k_sizes)
+        sk, sv = k_perm, v_perm
+        if g > 1 and getattr(cfg, "grouped_svg_ear_router", False):  # native K/V of each group
+            sk = _per_query_head(k_perm.reshape(b, h, n, d)[:, ::g].reshape(b * kvh, n, d), b, kvh, g)
+            sv = _per_query_head(v_perm.reshape(b, h, n, d)[:, ::g].reshape(b * kvh, n, d), b, kvh, g)
+        scores = svg_ear_value_error_scores(q_cent, sk, sv, k_cent, v_cent, k_sizes)
     else:
         scores = attention_mass_scores(q_cent, k_perm, k_sizes)
     if cfg.selector_budget_mode == "fixed_density":

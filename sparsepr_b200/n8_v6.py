@@ -506,16 +506,31 @@ class N8V6Core:
         batch, heads, tokens, dim = q_video.shape
         cfg = self.config
         cfg.validate(dim)
-        if int(gqa_group_size) != 1:
-            raise NotImplementedError("gqa_group_size > 1 is not implemented in sparsepr_b200.")
+        group = int(gqa_group_size)
+        if group <= 0 or heads % group:
+            raise ValueError(f"gqa_group_size must divide the query-head count; got H={heads}, G={group}.")
         if cfg.role_v_weight != 0.0:
             raise NotImplementedError("role_v_weight > 0 is not implemented in sparsepr_b200.")
         bh = batch * heads
+        kv_heads = heads // group
+        bkv = batch * kv_heads
         dev = q_video.device
         dt = torch.bfloat16
         q = q_video.to(dt).contiguous().view(bh, tokens, dim)
-        k = k_video.to(dt).contiguous().view(bh, tokens, dim)
-        v = v_video.to(dt).contiguous().view(bh, tokens, dim)
+        k_all = k_video.to(dt).contiguous()
+        v_all = v_video.to(dt).contiguous()
+        if group > 1:
+            # GQA (n8_v6.py:549-567): K/V are clustered once per native KV head
+            # (the first query head of each group); the key metric pools the
+            # queries of the whole group, sampling group x as many tokens.
+            k = k_all[:, ::group].contiguous().view(bkv, tokens, dim)
+            v = v_all[:, ::group].contiguous().view(bkv, tokens, dim)
+            k_metric_q = q.view(bkv, group * tokens, dim)
+        else:
+            k = k_all.view(bh, tokens, dim)
+            v = v_all.view(bh, tokens, dim)
+            k_metric_q = q
+        k_all, v_all = k_all.view(bh, tokens, dim), v_all.view(bh, tokens, dim)
         warm = self.initialized
         iters = cfg.kmeans_iter_step if warm else cfg.kmeans_iter_init
 
@@ -525,8 +540,8 @@ class N8V6Core:
                    or self.route_call_index % cfg.factor_refresh_every == 0)
         if refresh:
             k_factor, self.k_factor_state, self.k_factor_recovery_mask = self._updated_factor(
-                key_metric_from_queries(q, cfg.metric_sample_tokens), self.k_factor_state, self.k_factor_current,
-                cfg.role_k_rank)
+                key_metric_from_queries(k_metric_q, cfg.metric_sample_tokens * group), self.k_factor_state,
+                self.k_factor_current, cfg.role_k_rank)
         else:
             k_factor = self.k_factor_current
         self.k_factor_current = k_factor
@@ -538,15 +553,29 @@ class N8V6Core:
                 k_init_features = torch.bmm(self.k_centroids, k_factor) / k_scale
         if k_init_features is None:
             idx = (self.init_indices[0] if self.init_indices is not None
-                   else _init_indices(bh, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev))
+                   else _init_indices(bkv, tokens, cfg.num_k_centroids, cfg.kmeans_init_seed, dev))
             k_init_features = torch.gather(k_feat, 1, idx.unsqueeze(-1).expand(-1, -1, k_feat.shape[-1]))
         k_labels, _kc, k_sizes, k_off, k_order, k_it = K.kmeans_lloyd(k_feat, k_init_features, iters, cfg.kmeans_tol,
                                                                      precision=cfg.kmeans_precision)
 
         # Original-space K/V centroids fused with the K/V permute (n8_v6.py:734-741, 905-934).
         use_full = k_full_source is not None or v_full_source is not None
-        k_cent, k_perm = K.centroid_means(k, k_order, k_off, cfg.num_k_centroids, self.k_centroids, permute=not use_full)
-        v_cent, v_perm = K.centroid_means(v, k_order, k_off, cfg.num_k_centroids, self.v_centroids, permute=not use_full)
+        fused_perm = not use_full and group == 1
+        k_cent, k_perm = K.centroid_means(k, k_order, k_off, cfg.num_k_centroids, self.k_centroids, permute=fused_perm)
+        v_cent, v_perm = K.centroid_means(v, k_order, k_off, cfg.num_k_centroids, self.v_centroids, permute=fused_perm)
+        k_sizes_native = k_sizes
+        if group > 1:
+            # Native-head clustering copied to every query head of its group
+            # (n8_v6.py:808-834); each query head then permutes its own K/V
+            # rows with the group's order (n8_v6.py:905-934).
+            def per_query_head(t):
+                return t.view(batch, kv_heads, *t.shape[1:]).repeat_interleave(group, dim=1).reshape(
+                    bh, *t.shape[1:]).contiguous()
+
+            k_labels, k_sizes, k_off, k_order = (per_query_head(t) for t in (k_labels, k_sizes, k_off, k_order))
+            if not use_full:
+                k_perm = K.permute_rows(k_all, k_order)
+                v_perm = K.permute_rows(v_all, k_order)
         if use_full:
             if k_full_source is None or v_full_source is None:
                 raise ValueError("k_full_source and v_full_source must be provided together.")
@@ -566,11 +595,13 @@ class N8V6Core:
         # Query role factor from the key-centroid metric, row-RMS features (n8_v6.py:744-806).
         if refresh:
             q_factor, self.q_factor_state, self.q_factor_recovery_mask = self._updated_factor(
-                query_metric_from_key_centroids(k_cent, k_sizes), self.q_factor_state, self.q_factor_current,
+                query_metric_from_key_centroids(k_cent, k_sizes_native), self.q_factor_state, self.q_factor_current,
                 cfg.role_q_rank)
         else:
             q_factor = self.q_factor_current
         self.q_factor_current = q_factor
+        if group > 1:  # n8_v6.py:762-769: the group's Q factor on each query head
+            q_factor = q_factor.view(batch, kv_heads, dim, -1).repeat_interleave(group, dim=1).reshape(bh, dim, -1)
         with _MatmulPrecision(cfg.role_kv_matmul_precision):
             q_feat = torch.bmm(q.float(), q_factor)
             q_feat = (q_feat / q_feat.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)).contiguous()
@@ -587,8 +618,20 @@ class N8V6Core:
         self.q_centroids = q_cent
 
         # Selector scores, budgets and the cluster-pair map (n8_v6.py:957-1112).
+        if group > 1:
+            k_cent_rt = k_cent.view(batch, kv_heads, -1, dim).repeat_interleave(group, dim=1).reshape(bh, -1, dim)
+            v_cent_rt = v_cent.view(batch, kv_heads, -1, dim).repeat_interleave(group, dim=1).reshape(bh, -1, dim)
+        else:
+            k_cent_rt, v_cent_rt = k_cent, v_cent
         if cfg.selector_policy == "svg_ear_value":  # n8_v6.py:984-998 (no Jensen term)
-            scores = K.svg_ear_value_scores(q_cent, k_perm, v_perm, k_cent, v_cent, k_off)
+            sk, sv = k_perm, v_perm
+            if group > 1 and cfg.grouped_svg_ear_router:
+                # n8_v6.py:936-971: every query head of a group is scored
+                # against the group's native (first-head) sorted K/V.
+                t = k_perm.shape[1]
+                sk = k_perm.view(batch, heads, t, dim)[:, ::group].repeat_interleave(group, dim=1).reshape(bh, t, dim)
+                sv = v_perm.view(batch, heads, t, dim)[:, ::group].repeat_interleave(group, dim=1).reshape(bh, t, dim)
+            scores = K.svg_ear_value_scores(q_cent, sk, sv, k_cent_rt, v_cent_rt, k_off)
         else:  # attention_mass, n8_v6.py:971-983
             scores = K.attention_mass_scores(q_cent, k_perm, k_off)
         total_keys = int(total_key_tokens) if total_key_tokens is not None else tokens
@@ -602,7 +645,7 @@ class N8V6Core:
             budgets = torch.full((bh, cfg.num_q_centroids), budget, device=dev, dtype=torch.int32)
             base_density = budget / float(tokens)
         else:
-            budgets = _svg_top_p_key_budgets(q_cent, k_cent, k_sizes, cfg.svg_ear_top_p)
+            budgets = _svg_top_p_key_budgets(q_cent, k_cent_rt, k_sizes, cfg.svg_ear_top_p)
             budgets = budgets.clamp(min=int(math.ceil(cfg.adaptive_budget_min_density * tokens)),
                                     max=int(math.floor(cfg.adaptive_budget_max_density * tokens))).to(torch.int32)
             pair = (budgets.long() * q_sizes.long()).sum(dim=1).float() / float(tokens * tokens)

@@ -23,6 +23,10 @@ The attention step is the reference's ``dynamic_block_sparse_fwd_torch``
 (``kmeans_utils.py:1748-1841``) and ``apply_inverse_permutation``
 (1687-1695); repair is ``N8V6Core.repair``'s CPU branch.  Output:
 ``tests/golden/config0_<mode>.pt``.
+
+A GQA case (4 query heads, ``gqa_group_size=2``, K/V heads that differ
+within a group) records the reference route's labels, sizes, K/V centroids,
+Q factor features and map: ``tests/golden/config0_gqa.pt``.
 """
 
 from __future__ import annotations
@@ -121,6 +125,31 @@ def main(ref_root: str) -> None:
         print(mode, "k_iters", route.k_kmeans_iters, "q_iters", route.q_kmeans_iters,
               "density", info["effective_video_density"])
 
+    q, k, v = synthetic_qkv(4, 64, (4, 8, 8), dtype=torch.float32, seeds=(3, 4, 5))
+    calls["n"] = 0
+    cfg = n8.N8V6Config(
+        num_q_centroids=16, num_k_centroids=32, target_density=0.25,
+        kmeans_iter_init=8, kmeans_iter_step=2, probe_rows=16, repair_rank=16,
+        selector_policy="attention_mass", selector_budget_mode="fixed_density",
+        compile_role_kv_projection=False,
+    )
+    core = n8.N8V6Core(cfg)
+    route = core.route(q, k, v, gqa_group_size=2, total_key_tokens=q.shape[2])
+    torch.save({
+        "q": q, "k": k, "v": v, "gqa_group_size": 2,
+        "config": {"num_q_centroids": 16, "num_k_centroids": 32, "target_density": 0.25,
+                   "kmeans_iter_init": 8, "probe_rows": 16, "tol": 1e-4, "seed_k": seeds["k"]},
+        "q_labels": route.q_labels.clone(), "k_labels": route.k_labels.clone(),
+        "q_sizes": route.q_cluster_sizes.clone(), "k_sizes": route.k_cluster_sizes.clone(),
+        "k_centroids": core.k_centroids.clone(), "v_centroids": core.v_centroids.clone(),
+        "q_centroids": core.q_centroids.clone(), "mask": route.video_dynamic_map.clone(),
+        "q_features": route.q_role_features.clone(), "k_permuted": route.k_permuted.clone(),
+        "q_iters": route.q_kmeans_iters, "k_iters": route.k_kmeans_iters,
+    }, os.path.join(HERE, "config0_gqa.pt"))
+    print("gqa", "k_iters", route.k_kmeans_iters, "q_iters", route.q_kmeans_iters)
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPARSEPR_REFERENCE", ""))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py /path/to/SparsePR")
+    main(sys.argv[1])

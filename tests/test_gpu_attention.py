@@ -154,6 +154,52 @@ def test_route_matches_oracle(cuda, policy):
     assert torch.equal(r.video_dynamic_map.cpu(), routed[:, 1:, 1:])
 
 
+@pytest.mark.parametrize("policy,grouped", [("attention_mass", False), ("svg_ear_value", False),
+                                             ("svg_ear_value", True)])
+def test_gqa_route_matches_oracle(cuda, policy, grouped):
+    """GQA routing (group 2 over 4 query heads): K/V clustered per native KV
+    head, labels shared by the group, each query head's own K/V permuted by
+    the group's order, scores per query head."""
+    cfg = _cfg(selector_policy=policy, grouped_svg_ear_router=grouped)
+    q, k, v = synthetic_qkv(4, 128, (4, 8, 16), dtype=torch.bfloat16)
+    g, bh = 2, 4
+    core = N8V6Core(cfg)
+    r = core.route(q.to(cuda), k.to(cuda), v.to(cuda), gqa_group_size=g)
+    ro = oracle.oracle_route(q, k, v, _oracle_cfg(cfg), init_seed=0, tol=0.0, gqa_group_size=g)
+    kl, ql = r.k_labels.cpu().long(), r.q_labels.cpu().long()
+    assert kl.shape == (bh, q.shape[2])
+    assert torch.equal(kl[0], kl[1]) and torch.equal(kl[2], kl[3])
+    agree_k = (kl == ro.k_labels).float().mean().item()
+    agree_q = (ql == ro.q_labels).float().mean().item()
+    assert agree_k > 0.97 and agree_q > 0.97, (agree_k, agree_q)
+    ks, qs = r.k_cluster_sizes.cpu().long(), r.q_cluster_sizes.cpu().long()
+    k3, q3, v3 = k.view(bh, -1, 128), q.view(bh, -1, 128), v.view(bh, -1, 128)
+    order = oracle.stable_label_order(kl)
+    assert torch.equal(r.k_sorted_indices.cpu().long(), order)
+    kperm, vperm = oracle.permute_rows(k3, order), oracle.permute_rows(v3, order)
+    assert torch.equal(r.k_permuted.view(bh, -1, 128).cpu(), kperm)
+    assert torch.equal(r.v_permuted.view(bh, -1, 128).cpu(), vperm)
+    qcent = oracle.original_centroids(q3, ql, qs)
+    torch.testing.assert_close(core.q_centroids.cpu(), qcent, atol=1e-5, rtol=1e-5)
+    # K/V centroids stay per native head (the first query head of each group).
+    kn, vn = k[:, ::g].reshape(2, -1, 128), v[:, ::g].reshape(2, -1, 128)
+    kcent = oracle.original_centroids(kn, kl[::g], ks[::g])
+    torch.testing.assert_close(core.k_centroids.cpu(), kcent, atol=1e-5, rtol=1e-5)
+    if policy == "svg_ear_value":
+        rep = lambda t: t.repeat_interleave(g, dim=0)
+        sk, sv = (rep(kperm[::g]), rep(vperm[::g])) if grouped else (kperm, vperm)
+        sc = oracle.svg_ear_value_error_scores(qcent, sk, sv, rep(kcent),
+                                               rep(oracle.original_centroids(vn, kl[::g], ks[::g])), ks)
+        fin = torch.isfinite(sc) & ~(ks == 1).unsqueeze(1).expand_as(sc)
+        torch.testing.assert_close(r.scores.cpu()[fin], sc[fin], atol=2e-3, rtol=0)
+    else:
+        sc = oracle.attention_mass_scores(qcent, kperm, ks)
+        fin = torch.isfinite(sc)
+        torch.testing.assert_close(r.scores.cpu()[fin], sc[fin], atol=2e-4, rtol=1e-5)
+    routed = oracle.select_budget(r.scores.cpu(), ks, r.budgets.cpu())
+    assert torch.equal(r.video_dynamic_map.cpu(), routed[:, 1:, 1:])
+
+
 def _route_view(r, bh):
     return types.SimpleNamespace(
         q_labels=r.q_labels.cpu().long(), q_sizes=r.q_cluster_sizes.cpu().long(),

@@ -134,3 +134,34 @@ def test_oracle_warm_factor_matches_reference():
         assert torch.equal(rec, c["recovered"])
         torch.testing.assert_close(b, c["basis"], atol=1e-5, rtol=1e-4)
         torch.testing.assert_close(f, c["factor"], atol=1e-5, rtol=1e-4)
+
+
+def test_gqa_route_matches_reference():
+    """GQA route (4 query heads, group 2) against the reference's own route."""
+    g = torch.load(os.path.join(GOLDEN, "config0_gqa.pt"))
+    cfg = _cfg("fixed_density")
+    r = oracle.oracle_route(g["q"], g["k"], g["v"], cfg, init_seed=g["config"]["seed_k"], tol=g["config"]["tol"],
+                            gqa_group_size=g["gqa_group_size"])
+    assert torch.equal(r.k_labels, g["k_labels"].long())
+    assert torch.equal(r.q_labels, g["q_labels"].long())
+    assert torch.equal(r.k_sizes, g["k_sizes"].long())
+    assert torch.equal(r.q_sizes, g["q_sizes"].long())
+    assert torch.equal(r.mask, g["mask"])
+    assert (r.k_iters, r.q_iters) == (g["k_iters"], g["q_iters"])
+    # K/V centroids stay per native KV head; the route's are per query head.
+    torch.testing.assert_close(r.k_centroids[::2], g["k_centroids"].float(), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(r.v_centroids[::2], g["v_centroids"].float(), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(r.q_centroids, g["q_centroids"].float(), atol=1e-5, rtol=1e-5)
+    # Each query head permutes its own K rows by the group's labels.  The
+    # reference's argsort is not stable, so rows are compared per cluster as
+    # sorted sets rather than in order.
+    ref_perm = g["k_permuted"].reshape(r.k_perm.shape)
+    offs = torch.cat((torch.zeros(4, 1, dtype=torch.long), r.k_sizes.cumsum(1)), 1)
+    for h in range(4):
+        for c in range(r.k_sizes.shape[1]):
+            a, b = int(offs[h, c]), int(offs[h, c + 1])
+            mine = r.k_perm[h, a:b]
+            ref = ref_perm[h, a:b]
+            assert torch.equal(mine[mine[:, 0].argsort()], ref[ref[:, 0].argsort()])
+    with pytest.raises(ValueError):
+        oracle.oracle_route(g["q"], g["k"], g["v"], cfg, gqa_group_size=3)
