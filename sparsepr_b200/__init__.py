@@ -5,6 +5,7 @@ Public API:
 * :class:`N8V6Config`, :class:`N8V6Core`, :class:`N8V6Route` — the routing +
   repair core (drop-in for ``sparsepr.models.common.n8_v6``).
 * :func:`sparse_attention` — the adapter-facing attention call.
+* :class:`RouteCache` — route reuse across steps and CFG branches.
 * :func:`batch_kmeans_Euclid`, :class:`FlashKMeans` — standalone batched k-means.
 * :mod:`sparsepr_b200.kernels` — tensor wrappers over the C ABI.
 """
@@ -19,6 +20,7 @@ from .attention import (  # noqa: F401
     make_n8_core,
     sparse_attention,
 )
+from .route_cache import RouteCache, RouteReuseConfig, route_action  # noqa: F401
 from .kmeans import FlashKMeans, batch_kmeans_Euclid  # noqa: F401
 from .kernels import wan_qkv_norm_rope_layout  # noqa: F401
 
