@@ -127,6 +127,31 @@ def _print_kernel_table(step, q, k, v, dev):
     print(f"{'total':72s} {'':6s} {total / 1e3:9.3f}")
 
 
+def _print_route_reuse(cfg, q, k, v, dev, args):
+    """Device time of a refreshed layer call and of a temporal-reuse call
+    (cached route, current Q/K/V) through ``RouteCache``; one JSON line.
+    A side measurement, not the bench line: the headline step routes fresh."""
+    from sparsepr_b200 import N8V6Core, RouteCache, RouteReuseConfig
+
+    cache = RouteCache(RouteReuseConfig(dense_first_steps=0, route_refresh_every=1 << 30))
+    core = N8V6Core(cfg)
+    times = {"refresh": [], "temporal_reuse": []}
+    for i in range(args.warmup + args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if i == 0:
+            cache.entries.clear()
+        a.record()
+        out, _, info = cache.attention(q, k, v, core, module_id=0, step=i)
+        b.record()
+        torch.cuda.synchronize(dev)
+        if i == 0 or i >= args.warmup:
+            times[info["route_action"]].append(a.elapsed_time(b))
+        del out, info
+    print(json.dumps({"route_reuse": {"refresh_ms": times["refresh"][0],
+                                      "reuse_ms": statistics.median(times["temporal_reuse"]),
+                                      "reuse_calls": len(times["temporal_reuse"]), "heads": q.shape[1]}}))
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -172,6 +197,9 @@ def run_b200(args):
 
     if args.kernel_table:
         _print_kernel_table(step, q, k, v, dev)
+        return
+    if args.route_reuse:
+        _print_route_reuse(cfg, q, k, v, dev, args)
         return
 
     # Eager pass: per-kernel events for the attention roofline and the launch count.
@@ -338,6 +366,8 @@ def main():
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
     ap.add_argument("--e2e-slots", type=int, default=8, help="concurrent graph slots (streams) in the e2e measurement")
+    ap.add_argument("--route-reuse", action="store_true",
+                    help="time a refreshed and a cached-route (temporal reuse) layer call instead of the bench line")
     ap.add_argument("--kernel-table", action="store_true",
                     help="print per-kernel device times of one layer (torch profiler) instead of the bench line")
     args = ap.parse_args()
