@@ -235,6 +235,7 @@ struct KmeansWs {
   float* bias;       // (B, base) per problem, then centroid-norm scratch (TMA path)
   int32_t* counts;   // per-(cluster, chunk) counts / starts of the label sort
   float* next;       // updated centroids
+  float* caug;       // augmented centroid rows of the folded-bias assignment (may be empty)
 };
 
 static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
@@ -249,6 +250,8 @@ static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
   w.bias = w.xmax + bh;
   w.counts = c.take<int32_t>((size_t)bh * k * sort_chunks(n));
   w.next = c.take<float>((size_t)bh * k * d);
+  const size_t naug = d > 0 ? centroid_aug_count(bh, d, k) : 0;
+  w.caug = naug ? c.take<float>(naug) : nullptr;
   return w;
 }
 
@@ -339,7 +342,7 @@ extern "C" int spr_kmeans_assign(const void* x, int x_dtype, int64_t bh, int64_t
   cudaStream_t st = (cudaStream_t)stream;
   cudaMemsetAsync(w.err, 0, sizeof(int), st);
   if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st))) return s;
-  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, precision, labels, nullptr, w.err, st);
+  return launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, w.caug, precision, labels, nullptr, w.err, st);
 }
 
 extern "C" int spr_label_sort(const int32_t* labels, int64_t bh, int64_t n, int k, int32_t* sizes,
@@ -377,7 +380,7 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
   const int64_t count = bh * k * (int64_t)d;
   if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st))) return s;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, precision, labels, done, w.err, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, w.caug, precision, labels, done, w.err, st))) return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))

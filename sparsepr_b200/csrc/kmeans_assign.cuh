@@ -425,22 +425,39 @@ static int launch_assign_dp(const void* x, int64_t bh, int64_t n, int d, int k, 
 //
 // |x|^2 is computed by the argmin threads from the staged point tile.
 //
+// Folded bias (FOLD, when round_up(d, 8) + 8 <= DP): the FFMA and the |c|^2
+// shared-memory reads leave the epilogue.  The centroid operand is the
+// augmented row [-2c | 0.. | hi, lo, 0 x 6] (centroid_bias_kernel writes it,
+// feature dh = round_up(d, 8) holds hi = tf32(|c|^2 + B), dh + 1 the
+// remainder lo), and one extra K step multiplies those 8 features by a
+// constant all-ones A tile in shared memory, so the accumulator is s itself.
+// Scaling by -2 is exact; hi + lo carry |c|^2 + B to ~2^-21 relative, far
+// inside the TF32 error of the dot product.
+//
 // Warps 0-7: argmin (thread = point when MT == 2; two threads per point, one
 // per 64-column half, when MT == 1), warp 8: MMA issuer, warp 9: TMA producer.
 constexpr int kTmaAsgThreads = 320;
 
+// Features before the folded-bias columns, and the augmented row length.
+inline int fold_head(int d) { return (d + 7) / 8 * 8; }
+__device__ __forceinline__ int fold_head_dev(int d) { return (d + 7) / 8 * 8; }
+inline int fold_row(int d) { return fold_head(d) + 8; }
 template <int DP>
+inline bool assign_folds(int d) { return fold_row(d) <= DP; }
+
+template <int DP, bool FOLD = false>
 struct TmaAsg {
   static constexpr int kMT = DP <= 64 ? 2 : 1;   // 128-point M tiles per item
   static constexpr int kBlocks = DP / 32;         // 128-byte column blocks per row
   static constexpr int kTileBytes = 128 * DP * 4; // one 128-row tile of points or centroids
   static constexpr int kXBytes = kMT * kTileBytes;
-  static constexpr int kBudget = 216 * 1024;
+  static constexpr int kOnesBytes = FOLD ? 128 * 128 : 0;  // all-ones A tile (128 rows x 128 bytes)
+  static constexpr int kBudget = 216 * 1024 - kOnesBytes;
   static constexpr int kNX = (1024 + 2 * kXBytes + 2 * kTileBytes <= kBudget) ? 2 : 1;
   static constexpr int kNC = (1024 + kNX * kXBytes + 4 * kTileBytes <= kBudget)   ? 4
                              : (1024 + kNX * kXBytes + 3 * kTileBytes <= kBudget) ? 3
                                                                                   : 2;
-  static constexpr int kTotal = 1024 + kNX * kXBytes + kNC * kTileBytes;
+  static constexpr int kTotal = 1024 + kNX * kXBytes + kNC * kTileBytes + kOnesBytes;
   static constexpr int kCG = 2 / kMT;  // argmin threads per point
   static constexpr int kNQ = 8;        // |c|^2 ring slots
 };
@@ -482,10 +499,15 @@ __global__ void point_sqmax_kernel(const float* __restrict__ x, int64_t n, int d
 // maximum into cmax[b]; the last block of a problem (ticket counter) adds B to
 // the whole row and resets cmax[b] and the counter to 0 for the next call.
 // cmax and count must be zero before the first call.
+//
+// With caug (folded bias), row i of caug[b] ([k][fold_row(d)]) becomes
+// [-2c_i | 0 | hi_i, lo_i, 0 x 6], hi_i = tf32(|c_i|^2 + B) (low 13 bits
+// cleared) and lo_i = |c_i|^2 + B - hi_i; the last block writes hi and lo.
 __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restrict__ c, int k, int d, int kpad,
                                                             const float* __restrict__ xmax, float* __restrict__ csqb,
                                                             float* __restrict__ bias, float* __restrict__ cmax,
-                                                            unsigned* __restrict__ count, const int* __restrict__ done) {
+                                                            unsigned* __restrict__ count, const int* __restrict__ done,
+                                                            float* __restrict__ caug) {
   if (done && *done) return;
   __shared__ float s_max[4];
   __shared__ bool s_last;
@@ -503,6 +525,15 @@ __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restr
       s = fmaf(v.w, v.w, s);
     }
     out[i] = s;
+    if (caug) {
+      const int dh = fold_head_dev(d);
+      float4* w = reinterpret_cast<float4*>(caug + (b * k + i) * (dh + 8));
+      for (int e = 0; e < d / 4; ++e) {
+        const float4 v = r[e];
+        w[e] = make_float4(-2.f * v.x, -2.f * v.y, -2.f * v.z, -2.f * v.w);
+      }
+      for (int e = d / 4; e < dh / 4; ++e) w[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   float m = s;
 #pragma unroll
@@ -520,7 +551,17 @@ __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restr
   __threadfence();
   const float cm = __int_as_float(atomicAdd(reinterpret_cast<int*>(cmax + b), 0));
   const float B = fmaf(__ldcg(xmax + b), 1.0078125f, 0.25f * cm) + 1e-30f;
-  for (int j = threadIdx.x; j < kpad; j += blockDim.x) out[j] = j < k ? __ldcg(out + j) + B : 0.f;
+  for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
+    const float v = j < k ? __ldcg(out + j) + B : 0.f;
+    out[j] = v;
+    if (caug && j < k) {
+      const int dh = fold_head_dev(d);
+      const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+      float4* w = reinterpret_cast<float4*>(caug + (b * k + j) * (dh + 8) + dh);
+      w[0] = make_float4(hi, v - hi, 0.f, 0.f);
+      w[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   if (threadIdx.x == 0) {
     bias[2 * b] = B;
     bias[2 * b + 1] = B * 0.00390625f;
@@ -529,12 +570,12 @@ __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restr
   }
 }
 
-template <int DP>
+template <int DP, bool FOLD>
 __global__ void __launch_bounds__(kTmaAsgThreads, 1)
 assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap, int64_t n,
                   int d, int k, int64_t items, const float* __restrict__ csqb, const float* __restrict__ bias,
                   int32_t* __restrict__ labels, const int* __restrict__ done, int* __restrict__ err) {
-  using L = TmaAsg<DP>;
+  using L = TmaAsg<DP, FOLD>;
   constexpr int MT = L::kMT, NX = L::kNX, NC = L::kNC, NQ = L::kNQ, CG = L::kCG;
   constexpr int kBlocksPerThread = 4 / CG;  // 32-column TMEM blocks scanned per tile
   if (done && *done) return;
@@ -549,7 +590,13 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sx0 = tc::smem_addr(smem);
   const uint32_t sc0 = sx0 + NX * L::kXBytes;
+  const uint32_t sones = sc0 + NC * L::kTileBytes;  // FOLD: all-ones A tile
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if constexpr (FOLD) {
+    float4* o = reinterpret_cast<float4*>(smem + NX * L::kXBytes + NC * L::kTileBytes);
+    for (int i = tid; i < L::kOnesBytes / 16; i += kTmaAsgThreads) o[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+    tc::fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
+  }
   const int ctiles = (k + kAsgN - 1) / kAsgN;
   const int64_t ptiles = (n + MT * kAsgM - 1) / (MT * kAsgM);
 
@@ -611,15 +658,18 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         for (int t = 0; t < ctiles; ++t) {
           const int st = (int)(nc % NC), q = (int)(nc % NQ);
           if (nc >= NC && !(ok = tc::mbar_wait(&bar_c_empty[st], (uint32_t)(((nc / NC) - 1) & 1), err, 32))) break;
-          if (nc >= NQ && !(ok = tc::mbar_wait(&bar_q_read[q], (uint32_t)(((nc / NQ) - 1) & 1), err, 32))) break;
+          if (!FOLD && nc >= NQ && !(ok = tc::mbar_wait(&bar_q_read[q], (uint32_t)(((nc / NQ) - 1) & 1), err, 32)))
+            break;
           const uint32_t cbase = sc0 + st * L::kTileBytes;
           tc::mbar_expect_tx(&bar_c_full[st], (uint32_t)L::kTileBytes);
 #pragma unroll
           for (int j = 0; j < L::kBlocks; ++j)
             tc::tma_load_3d(cbase + j * (kAsgN * 128), &cmap, 32 * j, t * kAsgN, b, &bar_c_full[st]);
-          tc::mbar_expect_tx(&bar_q_full[q], kAsgN * 4);
-          tc::bulk_load(tc::smem_addr(&s_csq[q][0]), csqb + ((int64_t)b * ctiles + t) * kAsgN, kAsgN * 4,
-                        &bar_q_full[q]);
+          if constexpr (!FOLD) {
+            tc::mbar_expect_tx(&bar_q_full[q], kAsgN * 4);
+            tc::bulk_load(tc::smem_addr(&s_csq[q][0]), csqb + ((int64_t)b * ctiles + t) * kAsgN, kAsgN * 4,
+                          &bar_q_full[q]);
+          }
           ++nc;
         }
       }
@@ -628,13 +678,17 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
       for (int u = nx > NX ? nx - NX : 0; u < nx; ++u) tc::mbar_drain(&bar_x_full[u % NX], (u / NX) & 1);
       for (int64_t u = nc > NC ? nc - NC : 0; u < nc; ++u)
         tc::mbar_drain(&bar_c_full[u % NC], (uint32_t)((u / NC) & 1));
-      for (int64_t u = nc > NQ ? nc - NQ : 0; u < nc; ++u)
-        tc::mbar_drain(&bar_q_full[u % NQ], (uint32_t)((u / NQ) & 1));
+      if constexpr (!FOLD)
+        for (int64_t u = nc > NQ ? nc - NQ : 0; u < nc; ++u)
+          tc::mbar_drain(&bar_q_full[u % NQ], (uint32_t)((u / NQ) & 1));
     }
   } else if (warp == 8) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const int ksteps = (d + 7) / 8;
+      // FOLD: the K step over features [dh, dh + 8) of the centroid row (hi, lo, zeros) against ones.
+      const uint32_t kbf = (uint32_t)ksteps * 32;
+      const uint32_t offf = (kbf >> 7) * (kAsgN * 128) + (kbf & 127);
       int64_t gt = 0;
       int il = 0;
       bool ok = true;
@@ -652,13 +706,16 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const uint32_t dt = tmem + (uint32_t)(db * MT + mt) * 128;
+            if constexpr (FOLD)
+              tc::mma_tf32(dt, tc::sw128_desc(sones, 16, 1024), tc::sw128_desc(cbase + offf, 16, 1024), kIdescAsg,
+                           false);
             // 8 tf32 (32 bytes) per MMA K step; steps wholly inside the zero
             // padding past d are skipped.
             for (int kk = 0; kk < ksteps; ++kk) {
               const uint32_t kb = kk * 32;
               const uint32_t off = (kb >> 7) * (kAsgM * 128) + (kb & 127);
               tc::mma_tf32(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
-                           tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, kk > 0);
+                           tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, FOLD || kk > 0);
             }
           }
           tc::mma_commit(&bar_d_full[db]);
@@ -712,7 +769,8 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         const int db = (int)(gt & 1);
         const int q = (int)(gt % NQ);
         ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_d_full[db], (uint32_t)((gt >> 1) & 1), err, 34));
-        ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_q_full[q], (uint32_t)((gt / NQ) & 1), err, 34));
+        if constexpr (!FOLD)
+          ok = ok && __all_sync(0xffffffffu, tc::mbar_wait(&bar_q_full[q], (uint32_t)((gt / NQ) & 1), err, 34));
         tc::tc_fence_after();
         const int k0 = t * kAsgN;
         if (ok) {
@@ -733,7 +791,21 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             // Four independent minimum chains (columns j mod 4); keys are
             // distinct per column, so the merged minimum is the same.
             uint32_t m0 = 0xffffffffu, m1 = 0xffffffffu, m2 = 0xffffffffu, m3 = 0xffffffffu;
-            if (full) {
+            if (FOLD && full) {  // s is the accumulator itself
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                m0 = min(m0, __float_as_uint(acc[j]) * 32u + kj[j]);
+                m1 = min(m1, __float_as_uint(acc[j + 1]) * 32u + kj[j + 1]);
+                m2 = min(m2, __float_as_uint(acc[j + 2]) * 32u + kj[j + 2]);
+                m3 = min(m3, __float_as_uint(acc[j + 3]) * 32u + kj[j + 3]);
+              }
+            } else if (FOLD) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const uint32_t key = __float_as_uint(acc[j]) * 32u + kj[j];
+                m0 = j < lim ? min(m0, key) : m0;
+              }
+            } else if (full) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 const float4 c4 = *reinterpret_cast<const float4*>(cq + j);
@@ -759,7 +831,8 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
                 int first = 31;
 #pragma unroll
                 for (int j = 31; j >= 0; --j) {
-                  const uint32_t sq = __float_as_uint(fmaf(-2.f, acc[j], cq[j])) - __float_as_uint(base);
+                  const uint32_t sq = __float_as_uint(FOLD ? acc[j] : fmaf(-2.f, acc[j], cq[j])) -
+                                      __float_as_uint(base);
                   if (j < lim && sq <= thrq) first = j;
                 }
                 jj = first;
@@ -778,7 +851,7 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         }
         tc::tc_fence_before();
         tc::mbar_arrive(&bar_d_free[db]);
-        tc::mbar_arrive(&bar_q_read[q]);
+        if constexpr (!FOLD) tc::mbar_arrive(&bar_q_read[q]);
       }
       if constexpr (CG == 2) {
         // Merge the two column halves of each point (equal values: lower index).
@@ -809,16 +882,17 @@ inline int encode_row_map(CUtensorMap* m, const float* base, int d, int64_t rows
   return encode_map_3d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, d, rows, bh, 32, kAsgM, what);
 }
 
-template <int DP>
-static int launch_assign_tma(const float* x, int64_t bh, int64_t n, int d, int k, const float* c,
-                             const float* csqb, const float* bias, int32_t* labels, const int* done, int* err,
-                             cudaStream_t st) {
-  using L = TmaAsg<DP>;
+template <int DP, bool FOLD>
+static int launch_assign_tma_as(const float* x, int64_t bh, int64_t n, int d, int k, const float* c,
+                                const float* csqb, const float* bias, int32_t* labels, const int* done, int* err,
+                                cudaStream_t st) {
+  using L = TmaAsg<DP, FOLD>;
   CUtensorMap xmap, cmap;
   int s = encode_row_map(&xmap, x, d, n, bh, "points");
-  if (!s) s = encode_row_map(&cmap, c, d, k, bh, "centroids");
+  // FOLD: c is the augmented centroid array [bh][k][fold_row(d)].
+  if (!s) s = encode_row_map(&cmap, c, FOLD ? fold_row(d) : d, k, bh, "centroids");
   if (s) return s;
-  auto kern = assign_tma_kernel<DP>;
+  auto kern = assign_tma_kernel<DP, FOLD>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -827,6 +901,25 @@ static int launch_assign_tma(const float* x, int64_t bh, int64_t n, int d, int k
   const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
   kern<<<grid, kTmaAsgThreads, L::kTotal, st>>>(xmap, cmap, n, d, k, items, csqb, bias, labels, done, err);
   return check_launch("k-means assign (tcgen05, TMA)");
+}
+
+template <int DP>
+static int launch_assign_tma(const float* x, int64_t bh, int64_t n, int d, int k, const float* c, const float* caug,
+                             const float* csqb, const float* bias, int32_t* labels, const int* done, int* err,
+                             cudaStream_t st) {
+  if (caug && assign_folds<DP>(d))
+    return launch_assign_tma_as<DP, true>(x, bh, n, d, k, caug, csqb, bias, labels, done, err, st);
+  return launch_assign_tma_as<DP, false>(x, bh, n, d, k, c, csqb, bias, labels, done, err, st);
+}
+
+// Whether the TMA path folds the bias into the MMA for width d (the augmented
+// centroid rows are then needed), and their float count.  Only where the 8
+// extra features fit the tile width d already uses: widening the tile (d = 64
+// -> 96, one M tile per item) costs more than the fold saves.
+inline int assign_dp(int d) { return d <= 32 ? 32 : d <= 64 ? 64 : d <= 96 ? 96 : 128; }
+inline bool assign_fold_for(int d) { return fold_row(d) <= assign_dp(d); }
+inline size_t centroid_aug_count(int64_t bh, int d, int k) {
+  return assign_fold_for(d) ? (size_t)bh * (size_t)k * (size_t)fold_row(d) : 0;
 }
 
 // Padded |c|^2 entries needed by the TMA path: [bh][128 * centroid tiles].
@@ -857,22 +950,23 @@ inline int launch_point_sq(const void* x, int x_dtype, int precision, int64_t bh
 // statistics from launch_point_sq).  csq holds centroid_sq_pad_count floats,
 // bias 4 * bh: (B, base) pairs, then the centroid-norm maxima and counters of
 // centroid_bias_kernel (zeroed once per run by launch_point_sq).
+// caug: augmented centroid rows for the folded-bias TMA path
+// (centroid_aug_count floats; nullptr when that count is 0).
 inline int launch_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, const float* c,
-                         const float* xsq, const float* xmax, float* csq, float* bias, int precision, int32_t* labels,
-                         const int* done, int* err, cudaStream_t st) {
+                         const float* xsq, const float* xmax, float* csq, float* bias, float* caug, int precision,
+                         int32_t* labels, const int* done, int* err, cudaStream_t st) {
   if (assign_uses_tma(x_dtype, precision)) {
     const int kpad = (k + kAsgN - 1) / kAsgN * kAsgN;
-    centroid_bias_kernel<<<dim3((unsigned)(kpad / kAsgN), (unsigned)bh), 128, 0, st>>>(c, k, d, kpad, xmax, csq, bias,
-                                                                                     bias + 2 * bh,
-                                                                                     reinterpret_cast<unsigned*>(bias + 3 * bh),
-                                                                                     done);
+    if (!assign_fold_for(d)) caug = nullptr;
+    centroid_bias_kernel<<<dim3((unsigned)(kpad / kAsgN), (unsigned)bh), 128, 0, st>>>(
+        c, k, d, kpad, xmax, csq, bias, bias + 2 * bh, reinterpret_cast<unsigned*>(bias + 3 * bh), done, caug);
     int s = check_launch("centroid norms");
     if (s) return s;
     const float* xf = (const float*)x;
-    if (d <= 32) return launch_assign_tma<32>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
-    if (d <= 64) return launch_assign_tma<64>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
-    if (d <= 96) return launch_assign_tma<96>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
-    return launch_assign_tma<128>(xf, bh, n, d, k, c, csq, bias, labels, done, err, st);
+    if (d <= 32) return launch_assign_tma<32>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);
+    if (d <= 64) return launch_assign_tma<64>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);
+    if (d <= 96) return launch_assign_tma<96>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);
+    return launch_assign_tma<128>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);
   }
   const int64_t crows = bh * k;
   row_sq_kernel<<<(unsigned)((crows * 32 + 255) / 256), 256, 0, st>>>(c, crows, d, csq, done);
