@@ -306,6 +306,73 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_ulysses(args):
+    """Sequence-sharded variant (N > 1): each rank holds ``[1, N/W, H, D]`` of Q, K, V; per step
+    an NCCL all-to-all regroups them into head shards, the layer runs on the local heads and a
+    second all-to-all returns the output to sequence shards.  One JSON line (not the bench
+    line): step ms (max over ranks), the exchange's share, and an exactness check of the
+    exchange against direct head slices of the same tensors."""
+    import torch.distributed as dist
+
+    from sparsepr_b200 import N8V6Config, N8V6Core
+    from sparsepr_b200.sharding import reduce_step_stats
+    from sparsepr_b200.synthetic import synthetic_qkv
+    from sparsepr_b200.ulysses import UlyssesSparseAttention, head_to_seq, seq_to_head
+
+    world, rank, local = _dist()
+    if world < 2:
+        raise SystemExit("--ulysses needs torchrun with 2 or more ranks")
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    cfgd = CONFIGS[args.config]
+    grid, heads = cfgd["grid"], cfgd["heads"]
+    n = grid[0] * grid[1] * grid[2]
+    ns, hs = n // world, heads // world
+    # Every rank draws the same full tensors and keeps its sequence shard (BLHD).
+    full = synthetic_qkv(heads, 128, grid, dtype=torch.bfloat16, device=dev, seeds=(0, 1, 2))
+    shards = [t.permute(0, 2, 1, 3)[:, rank * ns:(rank + 1) * ns].contiguous() for t in full]
+    exact = all(torch.equal(seq_to_head(x), t[:, rank * hs:(rank + 1) * hs]) for x, t in zip(shards, full))
+    exact = exact and torch.equal(head_to_seq(seq_to_head(shards[0])), shards[0])
+    del full
+    layer = UlyssesSparseAttention(N8V6Config(**SPARSE))
+    inner = layer.attention
+    ev = []
+
+    def timed(q, k, v):  # the head-local layer, bracketed to separate it from the exchange
+        layer.core = N8V6Core(layer.core.config)  # cold call each step, like the bench line
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        o = inner(q, k, v)
+        b.record()
+        ev.append((a, b))
+        return o
+
+    layer.attention = timed
+    for _ in range(args.warmup):
+        layer(*shards)
+    torch.cuda.synchronize(dev)
+    ev.clear()
+    dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        out = layer(*shards)
+    t1.record()
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    layer_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    (ms, layer_ms), (ok,) = reduce_step_stats([ms, layer_ms], [0.0 if exact else 1.0], dev)
+    if rank == 0:
+        print(json.dumps({"ulysses": {
+            "n_gpus": world, "config": cfgd["name"], "tokens_per_rank": ns, "heads_per_rank": hs,
+            "ms_per_step": ms, "head_local_layer_ms": layer_ms, "exchange_ms": ms - layer_ms,
+            "exchange_bytes_per_rank": int(4 * 2 * ns * heads * 128 * (world - 1) / world),
+            "exchange_exact": ok == 0.0, "out_shape": list(out.shape), "timing": "eager, CUDA events, max over ranks"}}),
+            flush=True)
+    dist.destroy_process_group()
+
+
 def cpu_baseline(args, heads_sample: int = 2):
     """The oracle (CPU restatement of the reference algorithm) on a bounded sample:
     the same layer on ``heads_sample`` of the 40 heads, scaled to kept TFLOP/s."""
@@ -366,6 +433,8 @@ def main():
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
     ap.add_argument("--e2e-slots", type=int, default=8, help="concurrent graph slots (streams) in the e2e measurement")
+    ap.add_argument("--ulysses", action="store_true",
+                    help="(torchrun, N > 1) time the sequence-sharded Ulysses variant instead of the bench line")
     ap.add_argument("--route-reuse", action="store_true",
                     help="time a refreshed and a cached-route (temporal reuse) layer call instead of the bench line")
     ap.add_argument("--kernel-table", action="store_true",
@@ -373,6 +442,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.ulysses:
+        run_ulysses(args)
     else:
         run_b200(args)
 
