@@ -373,6 +373,88 @@ def run_ulysses(args):
     dist.destroy_process_group()
 
 
+def run_dit(args):
+    """Config 4: one denoising step of a random-init HunyuanVideo-architecture DiT
+    (hidden 3072, 24 x 128 heads, 20 double + 40 single blocks, bf16) on a 720p /
+    129-frame latent (33 x 45 x 80 = 118,800 video tokens) plus 256 text tokens, with
+    SparsePR (svg_ear_value scores, config-3 settings) on the video tokens of every
+    block.  N > 1 ranks shard the video tokens (Ulysses exchange around attention).
+    One JSON line (not the bench line)."""
+    import torch.distributed as dist
+
+    from sparsepr_b200 import N8V6Config
+    from sparsepr_b200.hunyuan_dit import HunyuanDiT, HunyuanDiTConfig, JointAttention, SparsePRBlocks
+    from sparsepr_b200.sharding import reduce_step_stats
+
+    world, rank, local = _dist()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    cfg = HunyuanDiTConfig()
+    model = HunyuanDiT(cfg, dev, seed=0)  # same seed on every rank: same weights
+    params = sum(w.numel() for w in _dit_tensors(model))
+    g = torch.Generator(device=dev).manual_seed(1)
+    latent = torch.randn(cfg.in_channels, 33, 90, 160, device=dev, generator=g)
+    text = torch.randn(256, cfg.text_dim, device=dev, generator=g)
+    pooled = torch.randn(cfg.vec_dim, device=dev, generator=g)
+    t, guidance = torch.tensor(900.0, device=dev), torch.tensor(6.0, device=dev)
+    sp = N8V6Config(**{**SPARSE, "selector_policy": "svg_ear_value"})
+    blocks = SparsePRBlocks(sp, cfg.double_blocks + cfg.single_blocks, prompt_length=256)
+    events = []
+    att = JointAttention(blocks, events=events)
+
+    def step():
+        blocks.reset()  # cold routing in every block, as on the first denoising step
+        return model.forward(latent, text, t, pooled, guidance, att, rank=rank, world=world)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    events.clear()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps)
+    with ClockSampler(dev.index) as clocks:
+        t0.record()
+        for _ in range(steps):
+            out = step()
+        t1.record()
+        torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    attn_ms = sum(a.elapsed_time(b) for a, b in events) / steps
+    (ms, attn_ms), _ = reduce_step_stats([ms, attn_ms], [0.0], dev)
+    if rank == 0:
+        n_video = 33 * 45 * 80
+        print(json.dumps({"dit": {
+            "workload": "HunyuanVideo-architecture DiT, one denoising step (config 4)", "n_gpus": world,
+            "ms_per_step": ms, "sparsepr_attention_ms": attn_ms, "attention_share": attn_ms / ms,
+            "video_tokens": n_video, "text_tokens": 256, "heads": cfg.heads, "blocks": cfg.double_blocks + cfg.single_blocks,
+            "params": params, "parallelism": f"video tokens sequence-sharded x{world} (Ulysses)" if world > 1 else "1 GPU",
+            "sparsepr": "svg_ear_value, 200/1000 clusters, 10 Lloyd iterations, keep 30%, repair (64 probes, rank 16)",
+            "data": "random-init bf16 weights, latent ~ N(0,1), text ~ N(0,1)", "out_tokens_per_rank": int(out.shape[0]),
+            "timing": "eager, CUDA events, max over ranks", "steps": steps, "clocks": clocks.summary()}}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _dit_tensors(model):
+    def walk(x):
+        if isinstance(x, torch.Tensor):
+            yield x
+        elif isinstance(x, (list, tuple)):
+            for y in x:
+                yield from walk(y)
+        elif isinstance(x, dict):
+            for y in x.values():
+                yield from walk(y)
+
+    for name, val in vars(model).items():
+        if name not in ("cfg", "device", "dtype"):
+            yield from walk(val)
+
+
 def cpu_baseline(args, heads_sample: int = 2):
     """The oracle (CPU restatement of the reference algorithm) on a bounded sample:
     the same layer on ``heads_sample`` of the 40 heads, scaled to kept TFLOP/s."""
@@ -428,7 +510,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS) + [4],
+                    help="3 (default) or 2: the SparsePR layer; 4: a HunyuanVideo-architecture DiT step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
@@ -444,6 +527,8 @@ def main():
         run_reference(args)
     elif args.ulysses:
         run_ulysses(args)
+    elif args.config == 4:
+        run_dit(args)
     else:
         run_b200(args)
 
