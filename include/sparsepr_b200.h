@@ -161,6 +161,22 @@ int spr_svg_ear_value_scores(const float* q_centroids, const void* k_sorted, con
                              void* stream);
 
 /*
+ * Role projection of the route (tensor cores): out[b,t,:] = x[b,t,:] F[b] / rms,
+ * x bf16 [bh,n,d] (d = 128), F fp32 [bh,d,r] (r = 16, 32, 48 or 64), out fp32
+ * [bh,n,r].  mode 0: one RMS over all n*r features of a head (clamped at
+ * 1e-8), written to scale[bh]; mode 1: one RMS per row (clamped at 1e-6),
+ * scale unused.  Workspace from spr_role_projection_workspace_bytes.
+ * Replaces the K-role projection + normalize_feature_scale and the Q-role
+ * role_projection_rms_triton (src/sparsepr/models/common/n8_v6.py:141-178,
+ * 659-806; src/sparsepr/kernels/triton/role_projection.py:58-103).
+ */
+size_t spr_role_projection_workspace_bytes(int64_t bh, int64_t n, int r);
+int spr_role_projection(const void* x, const float* factor, int64_t bh, int64_t n, int d, int r, int mode, float* out,
+                        float* scale, void* workspace, size_t workspace_bytes, void* stream);
+/* Status of the last spr_role_projection launch (synchronous copy; 0 = ok). */
+int spr_role_projection_status(int* out);
+
+/*
  * Status of the last spr_attention_mass_scores launch (synchronous copy):
  * *out = 0, or the code of a device-side bounded wait that gave up.
  */

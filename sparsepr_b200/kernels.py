@@ -224,6 +224,41 @@ def svg_ear_value_scores(q_centroids: torch.Tensor, k_sorted: torch.Tensor, v_so
     return scores
 
 
+def role_projection(x: torch.Tensor, factor: torch.Tensor, mode: str) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Role features of bf16 tokens x [B,N,128] with factor [B,128,r] (tensor cores, fp32 accuracy).
+
+    ``mode="global"``: divided by one RMS per problem, returns ``(feat, scale [B,1,1])``
+    (the K role); ``mode="row"``: divided by each row's RMS, returns ``(feat, None)``
+    (the Q role)."""
+    dev = _cuda(x, factor)
+    if x.dtype != torch.bfloat16 or x.dim() != 3:
+        raise RuntimeError(f"role projection expects bf16 [B,N,D] tokens, got {x.dtype} {tuple(x.shape)}")
+    b, n, d = x.shape
+    r = factor.shape[-1]
+    if tuple(factor.shape) != (b, d, r):
+        raise RuntimeError(f"role projection factor {tuple(factor.shape)} does not match tokens {tuple(x.shape)}")
+    if mode not in ("global", "row"):
+        raise ValueError(f"role projection mode must be 'global' or 'row', got {mode!r}")
+    f = factor.float().contiguous()
+    out = torch.empty((b, n, r), dtype=torch.float32, device=dev)
+    scale = torch.empty((b,), dtype=torch.float32, device=dev) if mode == "global" else None
+    nbytes = _lib.query("spr_role_projection_workspace_bytes", b, n, r)
+    ws = workspace(dev, nbytes, "role_projection")
+    _count(4 if mode == "global" else 2)
+    _lib.call("spr_role_projection", _p(_contig("x", x)), _p(f), b, n, d, r, 0 if mode == "global" else 1, _p(out),
+              _p(scale) if scale is not None else None, _p(ws), ws.numel(), _stream(dev))
+    return out, (scale.view(b, 1, 1) if scale is not None else None)
+
+
+def role_projection_error_code() -> int:
+    """Status word of the last role projection launch (0 = ok; synchronises)."""
+    import ctypes
+
+    v = ctypes.c_int(0)
+    _lib.call("spr_role_projection_status", ctypes.addressof(v))
+    return v.value
+
+
 def scores_error_code() -> int:
     """Status word of the last attention-mass scores launch (0 = ok; synchronises)."""
     import ctypes

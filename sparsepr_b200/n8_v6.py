@@ -203,6 +203,12 @@ def _init_indices(bh: int, tokens: int, k: int, seed: int, device) -> torch.Tens
                          lambda: random_init_indices(bh, tokens, k, seed).to(device))
 
 
+def _projection_kernel_fits(dim: int, rank: int) -> bool:
+    """Shapes served by the tensor-core role projection (``spr_role_projection``);
+    other shapes project with torch matmuls on the GPU."""
+    return dim == 128 and rank in (16, 32, 48, 64)
+
+
 def key_metric_from_queries(q: torch.Tensor, sample_tokens: int) -> torch.Tensor:
     """Uncentered fp32 covariance of sampled queries (``operator_kmeans.py:491-493``)."""
     pos = _sample_positions(q.shape[1], sample_tokens, q.device)
@@ -546,9 +552,12 @@ class N8V6Core:
             k_factor = self.k_factor_current
         self.k_factor_current = k_factor
         with _MatmulPrecision(cfg.role_kv_matmul_precision):
-            k_feat = torch.bmm(k.float(), k_factor)
-            k_scale = k_feat.square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(1e-8)
-            k_feat = (k_feat / k_scale).contiguous()
+            if _projection_kernel_fits(dim, k_factor.shape[-1]):
+                k_feat, k_scale = K.role_projection(k, k_factor, "global")
+            else:
+                k_feat = torch.bmm(k.float(), k_factor)
+                k_scale = k_feat.square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(1e-8)
+                k_feat = (k_feat / k_scale).contiguous()
             if k_init_features is None and warm:
                 k_init_features = torch.bmm(self.k_centroids, k_factor) / k_scale
         if k_init_features is None:
@@ -603,8 +612,11 @@ class N8V6Core:
         if group > 1:  # n8_v6.py:762-769: the group's Q factor on each query head
             q_factor = q_factor.view(batch, kv_heads, dim, -1).repeat_interleave(group, dim=1).reshape(bh, dim, -1)
         with _MatmulPrecision(cfg.role_kv_matmul_precision):
-            q_feat = torch.bmm(q.float(), q_factor)
-            q_feat = (q_feat / q_feat.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)).contiguous()
+            if _projection_kernel_fits(dim, q_factor.shape[-1]):
+                q_feat, _ = K.role_projection(q, q_factor, "row")
+            else:
+                q_feat = torch.bmm(q.float(), q_factor)
+                q_feat = (q_feat / q_feat.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)).contiguous()
             if q_init_features is None and warm:
                 qi = torch.bmm(self.q_centroids, q_factor)
                 q_init_features = qi / qi.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)

@@ -282,3 +282,22 @@ def test_chol_solve_matches_lapack(cuda, m, r):
     assert ((got - ref).abs().max() / ref.abs().max()).item() < 1e-4
     bad = -torch.eye(m).expand(1, m, m)  # not positive definite: non-finite, no error
     assert not torch.isfinite(K.chol_solve(bad.to(cuda), b[:1].to(cuda))).all()
+
+
+@pytest.mark.parametrize("r", [48, 64, 16])
+def test_role_projection_matches_fp64(cuda, r):
+    """Tensor-core role projection (bf16 tokens x 3-part bf16 split of the fp32
+    factor) against fp64: K role (one RMS per problem) and Q role (per-row RMS),
+    with a ragged last tile."""
+    g = torch.Generator().manual_seed(r)
+    x = torch.randn(3, 1000, 128, generator=g).bfloat16()
+    f = torch.randn(3, 128, r, generator=g) * 0.3
+    raw = torch.bmm(x.double(), f.double())
+    k_ref = raw / raw.square().mean(dim=(1, 2), keepdim=True).sqrt()
+    q_ref = raw / raw.square().mean(dim=2, keepdim=True).sqrt()
+    kf, ks = K.role_projection(x.to(cuda), f.to(cuda), "global")
+    qf, none = K.role_projection(x.to(cuda), f.to(cuda), "row")
+    assert K.role_projection_error_code() == 0 and none is None
+    torch.testing.assert_close(kf.cpu().double(), k_ref, atol=2e-6, rtol=2e-5)
+    torch.testing.assert_close(qf.cpu().double(), q_ref, atol=2e-6, rtol=2e-5)
+    torch.testing.assert_close(ks.cpu().view(-1).double(), raw.square().mean(dim=(1, 2)).sqrt(), rtol=1e-5, atol=0)
