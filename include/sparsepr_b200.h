@@ -161,6 +161,17 @@ int spr_svg_ear_value_scores(const float* q_centroids, const void* k_sorted, con
                              void* stream);
 
 /*
+ * Role-equal probe representatives: best[b,c] = the token of cluster c nearest
+ * (squared distance, ties to the lowest token) to the mean of the cluster's
+ * role features, n for an empty cluster.  feat fp32 [bh,n,r] (r <= 64), order
+ * int32 [bh,n] (tokens sorted by cluster, ascending within a cluster), offsets
+ * int32 [bh,k+1]; best int32 [bh,k].  Replaces the token pass of
+ * select_role_equal_probes_vectorized (src/sparsepr/.../residual_repair.py:118-208).
+ */
+int spr_probe_representatives(const float* feat, const int32_t* order, const int32_t* offsets, int64_t bh, int64_t n,
+                              int r, int k, int32_t* best, void* stream);
+
+/*
  * Role projection of the route (tensor cores): out[b,t,:] = x[b,t,:] F[b] / rms,
  * x bf16 [bh,n,d] (d = 128), F fp32 [bh,d,r] (r = 16, 32, 48 or 64), out fp32
  * [bh,n,r].  mode 0: one RMS over all n*r features of a head (clamped at

@@ -42,6 +42,7 @@ PROTOTYPES = {
     "spr_role_projection_workspace_bytes": (_SZ, [_I64, _I64, _I]),
     "spr_role_projection": (_I, [_P, _P, _I64, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "spr_role_projection_status": (_I, [_P]),
+    "spr_probe_representatives": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "spr_cholesky_qr": (_I, [_P, _I64, _I, _I, C.c_float, _P, _P, _P]),
     "spr_ridge_cholesky": (_I, [_P, _P, _I64, _I, C.c_float, C.c_float, _P, _P, _P]),
     "spr_svg_ear_value_scores_workspace_bytes": (_SZ, [_I64, _I, _I, _I64]),

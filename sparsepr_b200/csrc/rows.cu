@@ -99,6 +99,63 @@ __global__ void probe_scatter_kernel(const int32_t* __restrict__ rows, const uin
 
 using namespace spr;
 
+// Role-equal probe representatives (residual_repair.py:118-208, the heavy
+// token pass): per (head, cluster) the mean of the cluster's role features
+// and the token nearest to it (squared distance, ties to the lowest token
+// index; n for an empty cluster).  One warp per cluster walks the cluster's
+// tokens in sorted order (ascending token index within a cluster), lane l
+// holding features l and l + 32; the mean is summed in that fixed order.
+__global__ void probe_representatives_kernel(const float* __restrict__ feat, const int32_t* __restrict__ order,
+                                             const int32_t* __restrict__ offsets, int64_t n, int r, int k,
+                                             int64_t total, int32_t* __restrict__ best) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= total) return;
+  const int64_t b = w / k;
+  const int c = (int)(w % k);
+  const int32_t beg = offsets[b * (k + 1) + c], end = offsets[b * (k + 1) + c + 1];
+  if (end <= beg) {
+    if (lane == 0) best[w] = (int32_t)n;
+    return;
+  }
+  const bool has0 = lane < r, has1 = lane + 32 < r;
+  float m0 = 0.f, m1 = 0.f;
+  for (int32_t i = beg; i < end; ++i) {
+    const float* row = feat + (b * n + order[b * n + i]) * r;
+    if (has0) m0 += row[lane];
+    if (has1) m1 += row[lane + 32];
+  }
+  const float cnt = (float)(end - beg);
+  m0 = __fdiv_rn(m0, cnt);
+  m1 = __fdiv_rn(m1, cnt);
+  float best_d = INFINITY;
+  int32_t best_t = (int32_t)n;
+  for (int32_t i = beg; i < end; ++i) {
+    const int32_t t = order[b * n + i];
+    const float* row = feat + (b * n + t) * r;
+    float d0 = has0 ? row[lane] - m0 : 0.f, d1 = has1 ? row[lane + 32] - m1 : 0.f;
+    float d = fmaf(d0, d0, d1 * d1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (d < best_d || (d == best_d && t < best_t)) {
+      best_d = d;
+      best_t = t;
+    }
+  }
+  if (lane == 0) best[w] = best_t;
+}
+
+extern "C" int spr_probe_representatives(const float* feat, const int32_t* order, const int32_t* offsets, int64_t bh,
+                                         int64_t n, int r, int k, int32_t* best, void* stream) {
+  if (bh <= 0 || n <= 0 || n > INT32_MAX || k <= 0 || r <= 0 || r > 64)
+    return fail(SPR_ERR_SHAPE, "probe representatives: bh=%lld n=%lld r=%d k=%d unsupported (r <= 64)",
+                (long long)bh, (long long)n, r, k);
+  const int64_t total = bh * k;
+  probe_representatives_kernel<<<(unsigned)((total * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      feat, order, offsets, n, r, k, total, best);
+  return check_launch("probe representatives");
+}
+
 extern "C" int spr_version(void) { return 100; }
 extern "C" const char* spr_last_error(void) { return g_last_error; }
 

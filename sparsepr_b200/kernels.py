@@ -250,6 +250,22 @@ def role_projection(x: torch.Tensor, factor: torch.Tensor, mode: str) -> tuple[t
     return out, (scale.view(b, 1, 1) if scale is not None else None)
 
 
+def probe_representatives(feat: torch.Tensor, order: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    """Per (problem, cluster) the token nearest to the cluster's mean role feature
+    -> int32 [B,K] (N for an empty cluster); ``order``/``offsets`` from the k-means sort."""
+    dev = _cuda(feat, order, offsets)
+    b, n, r = feat.shape
+    k = offsets.shape[1] - 1
+    if tuple(order.shape) != (b, n) or order.dtype != torch.int32 or offsets.dtype != torch.int32:
+        raise RuntimeError(f"probe representatives: order {tuple(order.shape)} {order.dtype}, "
+                           f"offsets {tuple(offsets.shape)} {offsets.dtype} for features {tuple(feat.shape)}")
+    best = torch.empty((b, k), dtype=torch.int32, device=dev)
+    _count(1)
+    _lib.call("spr_probe_representatives", _p(_contig("feat", feat.float())), _p(_contig("order", order)),
+              _p(_contig("offsets", offsets)), b, n, r, k, _p(best), _stream(dev))
+    return best
+
+
 def role_projection_error_code() -> int:
     """Status word of the last role projection launch (0 = ok; synchronises)."""
     import ctypes

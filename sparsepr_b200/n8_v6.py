@@ -298,8 +298,13 @@ class _MatmulPrecision:
         torch.set_float32_matmul_precision(self.prev)
 
 
-def select_role_equal_probes(role_features, role_labels, num_clusters: int, rows: int):
-    """One representative per largest role group (``residual_repair.py:118-208``)."""
+def select_role_equal_probes(role_features, role_labels, num_clusters: int, rows: int, *, order=None,
+                             offsets=None):
+    """One representative per largest role group (``residual_repair.py:118-208``).
+
+    With the k-means sort (``order`` [BH,N] and ``offsets`` [BH,K+1], int32) the
+    token pass (cluster means of the role features and the nearest token) is one
+    kernel, ``spr_probe_representatives``, summing in a fixed order."""
     if role_features.ndim != 3 or role_labels.shape != role_features.shape[:2]:
         raise RuntimeError(
             "Role probe selection expects features [BH,N,R] and labels [BH,N], got "
@@ -313,19 +318,24 @@ def select_role_equal_probes(role_features, role_labels, num_clusters: int, rows
         )
     dev = role_features.device
     labels = role_labels.long()
-    feats = role_features.float()
-    sizes = torch.zeros((bh, num_clusters), device=dev, dtype=torch.long)
-    sizes.scatter_add_(1, labels, torch.ones_like(labels))
-    sums = torch.zeros((bh, num_clusters, r), device=dev, dtype=torch.float32)
-    sums.scatter_add_(1, labels.unsqueeze(2).expand(-1, -1, r), feats)
-    centers = sums / sizes.clamp_min(1).unsqueeze(2)
-    dist = (feats - torch.gather(centers, 1, labels.unsqueeze(2).expand(-1, -1, r))).square().sum(2)
-    best = torch.full((bh, num_clusters), float("inf"), device=dev)
-    best.scatter_reduce_(1, labels, dist, reduce="amin", include_self=True)
     tok = torch.arange(n, device=dev).view(1, -1).expand(bh, -1)
-    cand = torch.where(dist == torch.gather(best, 1, labels), tok, torch.full_like(tok, n))
-    best_idx = torch.full((bh, num_clusters), n, device=dev, dtype=torch.long)
-    best_idx.scatter_reduce_(1, labels, cand, reduce="amin", include_self=True)
+    if order is not None and offsets is not None and r <= 64 and offsets.shape[-1] == num_clusters + 1:
+        sizes = (offsets[:, 1:] - offsets[:, :-1]).long()
+        best_idx = K.probe_representatives(role_features, order.to(torch.int32).contiguous(),
+                                           offsets.to(torch.int32).contiguous()).long()
+    else:
+        feats = role_features.float()
+        sizes = torch.zeros((bh, num_clusters), device=dev, dtype=torch.long)
+        sizes.scatter_add_(1, labels, torch.ones_like(labels))
+        sums = torch.zeros((bh, num_clusters, r), device=dev, dtype=torch.float32)
+        sums.scatter_add_(1, labels.unsqueeze(2).expand(-1, -1, r), feats)
+        centers = sums / sizes.clamp_min(1).unsqueeze(2)
+        dist = (feats - torch.gather(centers, 1, labels.unsqueeze(2).expand(-1, -1, r))).square().sum(2)
+        best = torch.full((bh, num_clusters), float("inf"), device=dev)
+        best.scatter_reduce_(1, labels, dist, reduce="amin", include_self=True)
+        cand = torch.where(dist == torch.gather(best, 1, labels), tok, torch.full_like(tok, n))
+        best_idx = torch.full((bh, num_clusters), n, device=dev, dtype=torch.long)
+        best_idx.scatter_reduce_(1, labels, cand, reduce="amin", include_self=True)
     order = torch.argsort(sizes, dim=1, descending=True, stable=True)
     sel = torch.gather(best_idx, 1, order)[:, :count]
     sel = torch.where(sel < n, sel, tok[:, :count])
@@ -691,9 +701,13 @@ class N8V6Core:
         if route.probe_rows is not None and route.probe_weights is not None:
             rows, weights = route.probe_rows, route.probe_weights
         else:
-            selector = (select_first_token_largest_groups if cfg.probe_selection_policy == "first_token_largest_groups"
-                        else select_role_equal_probes)
-            rows, weights = selector(route.q_role_features, route.q_labels, cfg.num_q_centroids, cfg.probe_rows)
+            if cfg.probe_selection_policy == "first_token_largest_groups":
+                rows, weights = select_first_token_largest_groups(route.q_role_features, route.q_labels,
+                                                                  cfg.num_q_centroids, cfg.probe_rows)
+            else:
+                rows, weights = select_role_equal_probes(route.q_role_features, route.q_labels, cfg.num_q_centroids,
+                                                         cfg.probe_rows, order=route.q_sorted_indices,
+                                                         offsets=route.q_offsets)
             route.probe_rows, route.probe_weights = rows, weights
         count = int(rows.shape[1])
         q = q_video.to(torch.bfloat16).contiguous().view(bh, tokens, dim)
