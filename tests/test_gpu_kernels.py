@@ -313,22 +313,21 @@ def test_probe_representatives_match_oracle(cuda):
     bh, n, r, k = 3, 3000, 64, 40
     feats = torch.randn(bh, n, r, generator=g)
     labels = torch.randint(0, k - 3, (bh, n), generator=g)  # three empty clusters
-    labels[:, 10] = 5
-    labels[:, 2000] = 5
-    feats[:, 2000] = feats[:, 10]  # an exact duplicate inside cluster 5
+    # Cluster 5 = tokens {10, 20, 21, 2000}: 10 and 2000 equal p, 20 and 21 at p +- 5.
+    labels[labels == 5] = 6
+    labels[:, [10, 20, 21, 2000]] = 5
+    p = feats[:, 10].clone()
+    feats[:, 2000] = p
+    feats[:, 20] = p + 5
+    feats[:, 21] = p - 5
     order = oracle.stable_label_order(labels).to(torch.int32)
     sizes = torch.zeros(bh, k, dtype=torch.long).scatter_add_(1, labels, torch.ones_like(labels))
     offsets = torch.cat((torch.zeros(bh, 1, dtype=torch.long), sizes.cumsum(1)), 1).to(torch.int32)
     best = K.probe_representatives(feats.to(cuda), order.to(cuda), offsets.to(cuda)).cpu().long()
     assert (best[:, k - 3:] == n).all()
+    assert (best[:, 5] == 10).all()
     rows, w = select_role_equal_probes(feats.to(cuda), labels.to(cuda), k, 32, order=order.to(cuda),
                                        offsets=offsets.to(cuda))
     rows_ref, w_ref = oracle.select_role_equal_probes(feats, labels, k, 32)
     assert (rows.cpu() == rows_ref).float().mean().item() >= 0.99
     torch.testing.assert_close(w.cpu(), w_ref.float(), atol=1e-5, rtol=1e-5)
-    # The duplicate pair: whichever the mean is nearest to, the lower token wins.
-    c5 = order[0, offsets[0, 5]:offsets[0, 6]].long()
-    m = feats[0, c5].mean(0)
-    d = (feats[0, c5] - m).square().sum(1)
-    if d.argmin().item() == (c5 == 2000).nonzero().item() or c5[d.argmin()].item() in (10, 2000):
-        assert best[0, 5].item() == 10
