@@ -31,58 +31,79 @@ __global__ void permute_rows_kernel(const uint4* __restrict__ x, const int32_t* 
   }
 }
 
-// Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym)); one warp per
-// row, lane l owns dims l, l+32, l+64, l+96 (L and B are staged transposed so
-// the shared-memory reads are conflict free).
+// Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym))
+// (residual_repair.py:478-562).  One thread per row.  Per head the block
+// folds the standardisation into the left factor, L'[d][j] = L[d][j] / xs[d]
+// and c0[j] = -sum_d (xm[d] / xs[d]) L[d][j], so coords = v L' + c0; the row
+// streams in 16-byte chunks twice (coords, then the output; the second read
+// hits L1/L2) and the weights are shared-memory broadcasts (every lane of a
+// warp reads the same address).  ~4k FMAs per row, no shuffles.
 template <int D, int R>
 __global__ void __launch_bounds__(256)
 repair_apply_kernel(const __nv_bfloat16* __restrict__ base, const float* __restrict__ xm,
                     const float* __restrict__ xs, const float* __restrict__ ym, const float* __restrict__ left,
                     const float* __restrict__ basis, int64_t n, float alpha, __nv_bfloat16* __restrict__ out) {
-  __shared__ float sh_lt[R * D], sh_bt[R * D], sh_xm[D], sh_xs[D], sh_ym[D];
+  static_assert(R % 4 == 0 && D % 8 == 0, "repair apply tiling");
+  __shared__ float4 sh_l[D][R / 4], sh_b[D][R / 4];
+  __shared__ float sh_c0[R], sh_ym[D];
   const int64_t b = blockIdx.y;
-  for (int i = threadIdx.x; i < D * R; i += blockDim.x) {
-    const int dd = i / R, j = i % R;
-    sh_lt[j * D + dd] = left[b * D * R + i];
-    sh_bt[j * D + dd] = basis[b * D * R + i];
-  }
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    sh_xm[i] = xm[b * D + i];
-    sh_xs[i] = xs[b * D + i];
-    sh_ym[i] = ym[b * D + i];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) sh_ym[i] = ym[b * D + i];
+  float* lf = reinterpret_cast<float*>(sh_l);
+  float* bf = reinterpret_cast<float*>(sh_b);
+  for (int i = threadIdx.x; i < D * R; i += blockDim.x) {  // [d][j] layout, as stored
+    lf[i] = __fdiv_rn(left[b * D * R + i], xs[b * D + i / R]);
+    bf[i] = basis[b * D * R + i];
   }
   __syncthreads();
-  constexpr int PER = D / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int rows_per_block = blockDim.x >> 5;
-  for (int64_t r = (int64_t)blockIdx.x * rows_per_block + warp; r < n; r += (int64_t)gridDim.x * rows_per_block) {
-    const __nv_bfloat16* br = base + (b * n + r) * D;
-    float v[PER], z[PER];
+  if (threadIdx.x < R) {
+    float c = 0.f;
+    for (int d = 0; d < D; ++d) c = fmaf(-xm[b * D + d], lf[d * R + threadIdx.x], c);
+    sh_c0[threadIdx.x] = c;
+  }
+  __syncthreads();
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const uint4* row = reinterpret_cast<const uint4*>(base + (b * n + r) * D);
+  float coord[R];
 #pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int dd = lane + 32 * e;
-      v[e] = __bfloat162float(br[dd]);
-      z[e] = (v[e] - sh_xm[dd]) / sh_xs[dd];
+  for (int j = 0; j < R; ++j) coord[j] = sh_c0[j];
+#pragma unroll 2
+  for (int c = 0; c < D / 8; ++c) {
+    const uint4 u = row[c];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 v = __bfloat1622float2(h[e]);
+#pragma unroll
+      for (int q = 0; q < R / 4; ++q) {
+        const float4 l0 = sh_l[8 * c + 2 * e][q], l1 = sh_l[8 * c + 2 * e + 1][q];
+        coord[4 * q] = fmaf(v.y, l1.x, fmaf(v.x, l0.x, coord[4 * q]));
+        coord[4 * q + 1] = fmaf(v.y, l1.y, fmaf(v.x, l0.y, coord[4 * q + 1]));
+        coord[4 * q + 2] = fmaf(v.y, l1.z, fmaf(v.x, l0.z, coord[4 * q + 2]));
+        coord[4 * q + 3] = fmaf(v.y, l1.w, fmaf(v.x, l0.w, coord[4 * q + 3]));
+      }
     }
-    float coord[R];
+  }
+  uint4* orow = reinterpret_cast<uint4*>(out + (b * n + r) * D);
+#pragma unroll 2
+  for (int c = 0; c < D / 8; ++c) {
+    const uint4 u = row[c];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-    for (int j = 0; j < R; ++j) {
-      float p = 0.f;
+    for (int e = 0; e < 4; ++e) {
+      const float2 v = __bfloat1622float2(h[e]);
+      float c0 = sh_ym[8 * c + 2 * e], c1 = sh_ym[8 * c + 2 * e + 1];
 #pragma unroll
-      for (int e = 0; e < PER; ++e) p = fmaf(z[e], sh_lt[j * D + lane + 32 * e], p);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-      coord[j] = p;
+      for (int q = 0; q < R / 4; ++q) {
+        const float4 b0 = sh_b[8 * c + 2 * e][q], b1 = sh_b[8 * c + 2 * e + 1][q];
+        c0 = fmaf(coord[4 * q + 3], b0.w, fmaf(coord[4 * q + 2], b0.z, fmaf(coord[4 * q + 1], b0.y, fmaf(coord[4 * q], b0.x, c0))));
+        c1 = fmaf(coord[4 * q + 3], b1.w, fmaf(coord[4 * q + 2], b1.z, fmaf(coord[4 * q + 1], b1.y, fmaf(coord[4 * q], b1.x, c1))));
+      }
+      oh[e] = __floats2bfloat162_rn(fmaf(alpha, c0, v.x), fmaf(alpha, c1, v.y));
     }
-    __nv_bfloat16* orow = out + (b * n + r) * D;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) {
-      const int dd = lane + 32 * e;
-      float c = sh_ym[dd];
-#pragma unroll
-      for (int j = 0; j < R; ++j) c = fmaf(coord[j], sh_bt[j * D + dd], c);
-      orow[dd] = __float2bfloat16(v[e] + alpha * c);
-    }
+    orow[c] = o;
   }
 }
 
@@ -178,9 +199,7 @@ extern "C" int spr_repair_apply(const void* base, const float* x_mean, const flo
   if (d != 128 || r != 16) return fail(SPR_ERR_SHAPE, "repair apply: requires d=128, r=16 (got d=%d r=%d)", d, r);
   if (bh <= 0 || n <= 0 || bh > 65535) return fail(SPR_ERR_SHAPE, "repair apply: bad shape");
   cudaStream_t st = (cudaStream_t)stream;
-  // A few hundred rows per block amortise the per-block load of the 16 KB repair state.
-  const int64_t per_head = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (148 * 8 + bh - 1) / bh));
-  dim3 grid((unsigned)per_head, (unsigned)bh);
+  dim3 grid((unsigned)((n + 255) / 256), (unsigned)bh);  // one thread per row
   repair_apply_kernel<128, 16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)base, x_mean, x_scale, y_mean, left, basis,
                                                      n, alpha, (__nv_bfloat16*)out);
   int s = check_launch("repair apply");
