@@ -12,7 +12,9 @@ constexpr int kSortChunk = 2048;  // tokens per histogram / scatter chunk
 // Stable counting sort of labels.
 // ---------------------------------------------------------------------------
 
-// counts[b][c][chunk] = #tokens of cluster c in chunk `chunk` of problem b.
+// counts[b][chunk][c] = #tokens of cluster c in chunk `chunk` of problem b
+// (cluster-contiguous, so the histogram store, the scan and the scatter's
+// start loads are coalesced).
 __global__ void label_hist_kernel(const int32_t* __restrict__ labels, int64_t n, int k, int nchunks,
                                   int32_t* __restrict__ counts, const int* __restrict__ done) {
   if (done && *done) return;
@@ -27,7 +29,7 @@ __global__ void label_hist_kernel(const int32_t* __restrict__ labels, int64_t n,
   for (int64_t t = t0 + threadIdx.x; t < t1; t += blockDim.x) atomicAdd(&sh_cnt[lab[t]], 1);
   __syncthreads();
   int32_t* out = counts + (int64_t)b * k * nchunks;
-  for (int c = threadIdx.x; c < k; c += blockDim.x) out[(int64_t)c * nchunks + chunk] = sh_cnt[c];
+  for (int c = threadIdx.x; c < k; c += blockDim.x) out[(int64_t)chunk * k + c] = sh_cnt[c];
 }
 
 // Per problem: sizes, exclusive offsets and per-(cluster, chunk) start positions
@@ -47,8 +49,8 @@ __global__ void label_scan_kernel(int32_t* __restrict__ counts, int k, int nchun
   for (int c = c0; c < c1; ++c) {
     int32_t s = 0;
     for (int ch = 0; ch < nchunks; ++ch) {
-      int32_t v = cnt[(int64_t)c * nchunks + ch];
-      cnt[(int64_t)c * nchunks + ch] = s;  // exclusive within the cluster
+      int32_t v = cnt[(int64_t)ch * k + c];
+      cnt[(int64_t)ch * k + c] = s;  // exclusive within the cluster
       s += v;
     }
     sizes[b * k + c] = s;
@@ -66,7 +68,7 @@ __global__ void label_scan_kernel(int32_t* __restrict__ counts, int k, int nchun
   int32_t base = sh_part[threadIdx.x] - local;
   for (int c = c0; c < c1; ++c) {
     offsets[b * (k + 1) + c] = base;
-    for (int ch = 0; ch < nchunks; ++ch) cnt[(int64_t)c * nchunks + ch] += base;
+    for (int ch = 0; ch < nchunks; ++ch) cnt[(int64_t)ch * k + c] += base;
     base += sizes[b * k + c];
   }
   if (threadIdx.x == blockDim.x - 1) offsets[b * (k + 1) + k] = sh_part[threadIdx.x];
@@ -83,7 +85,7 @@ __global__ void label_scatter_kernel(const int32_t* __restrict__ labels, int64_t
   const int64_t b = blockIdx.y;
   const int lane = threadIdx.x;
   const int32_t* st = starts + b * (int64_t)k * nchunks;
-  for (int c = lane; c < k; c += 32) sh_cur[c] = st[(int64_t)c * nchunks + chunk];
+  for (int c = lane; c < k; c += 32) sh_cur[c] = st[(int64_t)chunk * k + c];
   __syncwarp();
   const int64_t t0 = (int64_t)chunk * kSortChunk;
   const int64_t t1 = min(n, t0 + kSortChunk);
@@ -154,14 +156,29 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
 #pragma unroll
   for (int i = 0; i < E; ++i) acc[i] = 0.f;
   if (active) {
-    for (int32_t s = beg + sub; s < end; s += rpw) {
-      const int32_t t = ob[s];
-      const uint4 v = reinterpret_cast<const uint4*>(xb + (int64_t)t * d)[ch];
-      if (x_perm) reinterpret_cast<uint4*>(x_perm + b * n * d + (int64_t)s * d)[ch] = v;
-      float f[E];
-      unpack16<T>(v, f);
+    // Four rows per lane group in flight: the indices first, then the rows
+    // (the gather is latency-bound), accumulated in token order.
+    constexpr int U = 4;
+    for (int32_t s0 = beg + sub; s0 < end; s0 += U * rpw) {
+      int32_t tt[U];
+      uint4 vv[U];
 #pragma unroll
-      for (int i = 0; i < E; ++i) acc[i] += f[i];
+      for (int u = 0; u < U; ++u) {
+        const int32_t s = s0 + u * rpw;
+        tt[u] = s < end ? ob[s] : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (tt[u] >= 0) vv[u] = reinterpret_cast<const uint4*>(xb + (int64_t)tt[u] * d)[ch];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (tt[u] < 0) break;
+        if (x_perm) reinterpret_cast<uint4*>(x_perm + b * n * d + (int64_t)(s0 + u * rpw) * d)[ch] = vv[u];
+        float f[E];
+        unpack16<T>(vv[u], f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) acc[i] += f[i];
+      }
     }
   }
   // Reduce the rpw row groups through shared memory in a fixed order.

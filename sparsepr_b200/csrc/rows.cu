@@ -124,14 +124,21 @@ using namespace spr;
 // token pass): per (head, cluster) the mean of the cluster's role features
 // and the token nearest to it (squared distance, ties to the lowest token
 // index; n for an empty cluster).  One warp per cluster walks the cluster's
-// tokens in sorted order (ascending token index within a cluster), lane l
-// holding features l and l + 32; the mean is summed in that fixed order.
-__global__ void probe_representatives_kernel(const float* __restrict__ feat, const int32_t* __restrict__ order,
-                                             const int32_t* __restrict__ offsets, int64_t n, int r, int k,
-                                             int64_t total, int32_t* __restrict__ best) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (w >= total) return;
+// tokens in sorted order (ascending token index within a cluster).  Mean:
+// lane l sums features l and l + 32 over the tokens in that fixed order.
+// Distances: lane j takes tokens j, j + 32, ... of the cluster and computes
+// each full distance against the mean in shared memory (no shuffles per
+// token); one warp argmin at the end.
+constexpr int kProbeWarps = 8;
+
+__global__ void __launch_bounds__(kProbeWarps * 32)
+probe_representatives_kernel(const float* __restrict__ feat, const int32_t* __restrict__ order,
+                             const int32_t* __restrict__ offsets, int64_t n, int r, int k, int64_t total,
+                             int32_t* __restrict__ best) {
+  __shared__ __align__(16) float sh_mean[kProbeWarps][64];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t w = (int64_t)blockIdx.x * kProbeWarps + wib;
+  if (w >= total) return;  // warp-uniform; no block-wide barrier below
   const int64_t b = w / k;
   const int c = (int)(w % k);
   const int32_t beg = offsets[b * (k + 1) + c], end = offsets[b * (k + 1) + c + 1];
@@ -139,28 +146,66 @@ __global__ void probe_representatives_kernel(const float* __restrict__ feat, con
     if (lane == 0) best[w] = (int32_t)n;
     return;
   }
+  const int32_t* ob = order + b * n;
+  const float* fb = feat + b * n * r;
   const bool has0 = lane < r, has1 = lane + 32 < r;
   float m0 = 0.f, m1 = 0.f;
-  for (int32_t i = beg; i < end; ++i) {
-    const float* row = feat + (b * n + order[b * n + i]) * r;
-    if (has0) m0 += row[lane];
-    if (has1) m1 += row[lane + 32];
+  for (int32_t i = beg; i < end; i += 4) {  // four rows in flight, summed in token order
+    float a0[4], a1[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      a0[u] = 0.f;
+      a1[u] = 0.f;
+      if (i + u < end) {
+        const float* row = fb + (int64_t)ob[i + u] * r;
+        if (has0) a0[u] = row[lane];
+        if (has1) a1[u] = row[lane + 32];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      m0 += a0[u];
+      m1 += a1[u];
+    }
   }
   const float cnt = (float)(end - beg);
-  m0 = __fdiv_rn(m0, cnt);
-  m1 = __fdiv_rn(m1, cnt);
+  sh_mean[wib][lane] = __fdiv_rn(m0, cnt);
+  sh_mean[wib][lane + 32] = __fdiv_rn(m1, cnt);
+  __syncwarp();
   float best_d = INFINITY;
   int32_t best_t = (int32_t)n;
-  for (int32_t i = beg; i < end; ++i) {
-    const int32_t t = order[b * n + i];
-    const float* row = feat + (b * n + t) * r;
-    float d0 = has0 ? row[lane] - m0 : 0.f, d1 = has1 ? row[lane + 32] - m1 : 0.f;
-    float d = fmaf(d0, d0, d1 * d1);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-    if (d < best_d || (d == best_d && t < best_t)) {
+  for (int32_t i = beg + lane; i < end; i += 32) {
+    const int32_t t = ob[i];
+    const float4* row = reinterpret_cast<const float4*>(fb + (int64_t)t * r);
+    const float4* mu = reinterpret_cast<const float4*>(sh_mean[wib]);
+    float d0 = 0.f, d1 = 0.f;
+    for (int q = 0; q < r / 4; q += 2) {
+      const float4 x0 = row[q], c0 = mu[q];
+      d0 = fmaf(x0.x - c0.x, x0.x - c0.x, d0);
+      d0 = fmaf(x0.y - c0.y, x0.y - c0.y, d0);
+      d0 = fmaf(x0.z - c0.z, x0.z - c0.z, d0);
+      d0 = fmaf(x0.w - c0.w, x0.w - c0.w, d0);
+      if (q + 1 < r / 4) {
+        const float4 x1 = row[q + 1], c1 = mu[q + 1];
+        d1 = fmaf(x1.x - c1.x, x1.x - c1.x, d1);
+        d1 = fmaf(x1.y - c1.y, x1.y - c1.y, d1);
+        d1 = fmaf(x1.z - c1.z, x1.z - c1.z, d1);
+        d1 = fmaf(x1.w - c1.w, x1.w - c1.w, d1);
+      }
+    }
+    const float d = d0 + d1;
+    if (d < best_d) {  // tokens of a lane ascend: strict keeps the lower one
       best_d = d;
       best_t = t;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float od = __shfl_xor_sync(0xffffffffu, best_d, o);
+    const int32_t ot = __shfl_xor_sync(0xffffffffu, best_t, o);
+    if (od < best_d || (od == best_d && ot < best_t)) {
+      best_d = od;
+      best_t = ot;
     }
   }
   if (lane == 0) best[w] = best_t;
@@ -171,9 +216,11 @@ extern "C" int spr_probe_representatives(const float* feat, const int32_t* order
   if (bh <= 0 || n <= 0 || n > INT32_MAX || k <= 0 || r <= 0 || r > 64)
     return fail(SPR_ERR_SHAPE, "probe representatives: bh=%lld n=%lld r=%d k=%d unsupported (r <= 64)",
                 (long long)bh, (long long)n, r, k);
+  if (r % 4) return fail(SPR_ERR_SHAPE, "probe representatives: r=%d must be a multiple of 4", r);
+  if (!aligned(feat, 16)) return fail(SPR_ERR_ALIGN, "probe representatives: features must be 16-byte aligned");
   const int64_t total = bh * k;
-  probe_representatives_kernel<<<(unsigned)((total * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      feat, order, offsets, n, r, k, total, best);
+  probe_representatives_kernel<<<(unsigned)((total + kProbeWarps - 1) / kProbeWarps), kProbeWarps * 32, 0,
+                                 (cudaStream_t)stream>>>(feat, order, offsets, n, r, k, total, best);
   return check_launch("probe representatives");
 }
 
