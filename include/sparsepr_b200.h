@@ -166,7 +166,7 @@ int spr_svg_ear_value_scores(const float* q_centroids, const void* k_sorted, con
  * role features, n for an empty cluster.  feat fp32 [bh,n,r] (r <= 64), order
  * int32 [bh,n] (tokens sorted by cluster, ascending within a cluster), offsets
  * int32 [bh,k+1]; best int32 [bh,k].  Replaces the token pass of
- * select_role_equal_probes_vectorized (src/sparsepr/.../residual_repair.py:118-208).
+ * select_role_equal_probes_vectorized (src/sparsepr/models/cosmos3/residual_repair.py:118-208).
  */
 int spr_probe_representatives(const float* feat, const int32_t* order, const int32_t* offsets, int64_t bh, int64_t n,
                               int r, int k, int32_t* best, void* stream);

@@ -32,7 +32,7 @@ __global__ void permute_rows_kernel(const uint4* __restrict__ x, const int32_t* 
 }
 
 // Repair: out = bf16(base + alpha*((((base - xm)/xs) L) B^T + ym))
-// (residual_repair.py:478-562).  One thread per row.  Per head the block
+// (kernels/triton/residual_repair.py:96-160, wrapper 478-562; one rounding).  One thread per row.  Per head the block
 // folds the standardisation into the left factor, L'[d][j] = L[d][j] / xs[d]
 // and c0[j] = -sum_d (xm[d] / xs[d]) L[d][j], so coords = v L' + c0; the row
 // streams in 16-byte chunks twice (coords, then the output; the second read
@@ -120,7 +120,7 @@ __global__ void probe_scatter_kernel(const int32_t* __restrict__ rows, const uin
 
 using namespace spr;
 
-// Role-equal probe representatives (residual_repair.py:118-208, the heavy
+// Role-equal probe representatives (models/cosmos3/residual_repair.py:118-208, the heavy
 // token pass): per (head, cluster) the mean of the cluster's role features
 // and the token nearest to it (squared distance, ties to the lowest token
 // index; n for an empty cluster).  One warp per cluster walks the cluster's
