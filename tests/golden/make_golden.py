@@ -27,6 +27,12 @@ The attention step is the reference's ``dynamic_block_sparse_fwd_torch``
 A GQA case (4 query heads, ``gqa_group_size=2``, K/V heads that differ
 within a group) records the reference route's labels, sizes, K/V centroids,
 Q factor features and map: ``tests/golden/config0_gqa.pt``.
+
+An SVG-EAR value-error case (``selector_policy="svg_ear_value"``, D = 128, the
+scorer's only width) runs the reference's own ``_svg_ear_value_error_kernel``
+(``svg_ear.py:95-193``) through Triton's CPU interpreter (``TRITON_INTERPRET=1``,
+launched as its wrapper ``svg_ear_value_error_scores_triton`` launches it,
+``svg_ear.py:453-531``) inside the route: ``tests/golden/config0_svg_value.pt``.
 """
 
 from __future__ import annotations
@@ -42,6 +48,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 
 
 def main(ref_root: str) -> None:
+    os.environ["TRITON_INTERPRET"] = "1"  # only the SVG-EAR case runs a Triton kernel (on CPU)
     sys.path.insert(0, os.path.join(ref_root, "src"))
     sys.path.insert(0, REPO)
     from flash_kmeans.torch_fallback import batch_kmeans_Euclid_torch_native
@@ -83,7 +90,26 @@ def main(ref_root: str) -> None:
                     out[h, :, c] = torch.logsumexp(lg, dim=1)
         return out
 
+    def svg_shim(*, qcentroids, k_sorted, v_sorted, kcentroids, vcentroids, kcluster_sizes, gqa_group,
+                 block_q, block_n, logical_tokens=None, **_):
+        import triton
+        from sparsepr.kernels.triton.svg_ear import _svg_ear_value_error_kernel
+
+        h, cq, d = qcentroids.shape
+        ck = kcluster_sizes.shape[1]
+        tokens = k_sorted.shape[1]
+        off = torch.cat((torch.zeros(h, 1, dtype=torch.int32), kcluster_sizes.int().cumsum(1).int()), 1).contiguous()
+        scores = torch.empty(h, cq, ck)
+        bq = min(block_q, 16)
+        _svg_ear_value_error_kernel[(triton.cdiv(cq, bq), ck, h)](
+            qcentroids.float().contiguous(), k_sorted.contiguous(), v_sorted.contiguous(),
+            kcentroids.float().contiguous(), vcentroids.float().contiguous(), kcentroids.float().contiguous(), off,
+            scores, Q_CLUSTERS=cq, K_CLUSTERS=ck, TOKENS=tokens, SORTED_HEAD_STRIDE=tokens, DIM=d,
+            GQA_GROUP=gqa_group, JENSEN_VAR_CAP=0.0, USE_JENSEN=False, BLOCK_Q=bq, BLOCK_N=min(block_n, 32))
+        return scores
+
     n8.batch_kmeans_Euclid = kmeans_shim
+    n8.svg_ear_value_error_scores_triton = svg_shim
     n8.permute_tensor_by_labels_triton = permute_shim
     n8.attention_mass_scores_triton = scores_shim
 
@@ -147,6 +173,27 @@ def main(ref_root: str) -> None:
         "q_iters": route.q_kmeans_iters, "k_iters": route.k_kmeans_iters,
     }, os.path.join(HERE, "config0_gqa.pt"))
     print("gqa", "k_iters", route.k_kmeans_iters, "q_iters", route.q_kmeans_iters)
+
+    q, k, v = synthetic_qkv(2, 128, (4, 8, 8), dtype=torch.float32, seeds=(6, 7, 8))
+    calls["n"] = 0
+    cfg = n8.N8V6Config(
+        num_q_centroids=16, num_k_centroids=32, target_density=0.25,
+        kmeans_iter_init=8, kmeans_iter_step=2, probe_rows=16, repair_rank=16,
+        selector_policy="svg_ear_value", selector_budget_mode="fixed_density",
+        compile_role_kv_projection=False,
+    )
+    core = n8.N8V6Core(cfg)
+    route = core.route(q, k, v, total_key_tokens=q.shape[2])
+    torch.save({
+        "q": q, "k": k, "v": v,
+        "config": {"num_q_centroids": 16, "num_k_centroids": 32, "target_density": 0.25,
+                   "kmeans_iter_init": 8, "probe_rows": 16, "tol": 1e-4, "seed_k": seeds["k"]},
+        "q_labels": route.q_labels.clone(), "k_labels": route.k_labels.clone(),
+        "q_sizes": route.q_cluster_sizes.clone(), "k_sizes": route.k_cluster_sizes.clone(),
+        "mask": route.video_dynamic_map.clone(),
+        "q_iters": route.q_kmeans_iters, "k_iters": route.k_kmeans_iters,
+    }, os.path.join(HERE, "config0_svg_value.pt"))
+    print("svg_value", "k_iters", route.k_kmeans_iters, "q_iters", route.q_kmeans_iters)
 
 
 if __name__ == "__main__":

@@ -165,3 +165,18 @@ def test_gqa_route_matches_reference():
             assert torch.equal(mine[mine[:, 0].argsort()], ref[ref[:, 0].argsort()])
     with pytest.raises(ValueError):
         oracle.oracle_route(g["q"], g["k"], g["v"], cfg, gqa_group_size=3)
+
+
+def test_svg_value_route_matches_reference():
+    """Route with the SVG-EAR value-error selector (the reference's default policy)
+    against the reference's own route, its Triton scorer run on the CPU."""
+    g = torch.load(os.path.join(GOLDEN, "config0_svg_value.pt"))
+    cfg = _cfg("fixed_density")
+    cfg.selector_policy = "svg_ear_value"
+    r = oracle.oracle_route(g["q"], g["k"], g["v"], cfg, init_seed=g["config"]["seed_k"], tol=g["config"]["tol"])
+    assert torch.equal(r.k_labels, g["k_labels"].long())
+    assert torch.equal(r.q_labels, g["q_labels"].long())
+    assert torch.equal(r.k_sizes, g["k_sizes"].long())
+    assert torch.equal(r.q_sizes, g["q_sizes"].long())
+    assert (r.k_iters, r.q_iters) == (g["k_iters"], g["q_iters"])
+    assert torch.equal(r.mask, g["mask"])
