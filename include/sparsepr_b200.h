@@ -186,12 +186,18 @@ int spr_role_projection(const void* x, const float* factor, int64_t bh, int64_t 
                         float* scale, void* workspace, size_t workspace_bytes, void* stream);
 /* Status of the last spr_role_projection launch (synchronous copy; 0 = ok). */
 int spr_role_projection_status(int* out);
+/* Stream-ordered copy of the same status word into device memory at dst (one
+ * int32), so a caller can collect it without synchronising. */
+int spr_role_projection_status_async(int32_t* dst, void* stream);
 
 /*
  * Status of the last spr_attention_mass_scores launch (synchronous copy):
  * *out = 0, or the code of a device-side bounded wait that gave up.
  */
 int spr_attention_mass_scores_status(int* out);
+/* Stream-ordered copy of the same status word into device memory at dst (one
+ * int32), so a caller can collect it without synchronising. */
+int spr_attention_mass_scores_status_async(int32_t* dst, void* stream);
 
 /*
  * Budgeted cluster selection per (b, q): descending score (ties -> lower
@@ -236,17 +242,34 @@ size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq);
  * result as spr_block_sparse_attn minus the workspace.  Its scratch is a fixed
  * library-owned device array of 65,536 tile-table entries: every GPU that loads
  * the library keeps 256 KiB for it until the process exits, and calls with
- * bh*(cq+1) > 65,536 are rejected with SPR_ERR_SHAPE.  The first call on a
- * device looks up the array's device address (do it before any stream
- * capture).  All calls share the array: calls that overlap on the GPU (other
- * streams, other host threads) race; the array keeps the last call's contents
- * and each call rewrites what it reads.  No counterpart in the reference.
+ * bh*(cq+1) > 65,536 are rejected with SPR_ERR_SHAPE.  Every call looks up
+ * the array's device address on the current device (cudaGetSymbolAddress).
+ * All calls share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race; the array keeps the last call's contents and each
+ * call rewrites what it reads.  No counterpart in the reference.
  */
 int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_perm, const void* v_perm,
                                   const int32_t* q_offsets, const int32_t* k_offsets,
                                   const int32_t* sel_ids, const int32_t* sel_counts,
                                   int64_t bh, int64_t nq, int64_t nk, int d, int cq, int ck,
                                   const int32_t* q_order, void* out, void* stream);
+
+/*
+ * Device status word of the last spr_block_sparse_attn_noalloc call on the
+ * current device (0 = ok, else the code of the bounded wait that gave up, in
+ * which case that call's output is incomplete).  Synchronous copy.  No
+ * counterpart in the reference (its kernels trap instead of reporting).
+ */
+int spr_block_sparse_attn_noalloc_status(int* out);
+
+/*
+ * Self-test of the bounded device wait used by every pipelined kernel here:
+ * one thread waits on an mbarrier that nothing completes, gives up after
+ * limit_ns (at most 0.1 s), writes `code` into the device int *err (if it is
+ * still 0) and the kernel returns; the context stays usable.  No counterpart
+ * in the reference (its kernels have no bounded waits).
+ */
+int spr_selftest_bounded_wait(int* err, int code, int64_t limit_ns, void* stream);
 
 /* ---------------------------------------------------------------- small linear algebra */
 

@@ -7,6 +7,7 @@ Public API:
 * :func:`sparse_attention` — the adapter-facing attention call.
 * :class:`RouteCache` — route reuse across steps and CFG branches.
 * :func:`batch_kmeans_Euclid`, :class:`FlashKMeans` — standalone batched k-means.
+* :func:`check_status` — raise if a device-side bounded wait of the last layer gave up.
 * :mod:`sparsepr_b200.kernels` — tensor wrappers over the C ABI.
 """
 
@@ -23,5 +24,17 @@ from .attention import (  # noqa: F401
 from .route_cache import RouteCache, RouteReuseConfig, route_action  # noqa: F401
 from .kmeans import FlashKMeans, batch_kmeans_Euclid  # noqa: F401
 from .kernels import wan_qkv_norm_rope_layout  # noqa: F401
+
+
+def check_status(device=None) -> None:
+    """Wait for the status words of the last SparsePR layer on ``device`` (default:
+    the current CUDA device) and raise ``RuntimeError`` if a device-side bounded
+    wait gave up during it."""
+    import torch
+
+    from .kernels import raise_device_status
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    raise_device_status(dev, wait=True)
 
 __version__ = "0.1.0"

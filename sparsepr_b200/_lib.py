@@ -39,9 +39,11 @@ PROTOTYPES = {
     "spr_permute_rows": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _I, _P]),
     "spr_attention_mass_scores": (_I, [_P, _P, _P, _I64, _I, _I, _I64, _I, _P, _P]),
     "spr_attention_mass_scores_status": (_I, [_P]),
+    "spr_attention_mass_scores_status_async": (_I, [_P, _P]),
     "spr_role_projection_workspace_bytes": (_SZ, [_I64, _I64, _I]),
     "spr_role_projection": (_I, [_P, _P, _I64, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "spr_role_projection_status": (_I, [_P]),
+    "spr_role_projection_status_async": (_I, [_P, _P]),
     "spr_probe_representatives": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _P, _P]),
     "spr_cholesky_qr": (_I, [_P, _I64, _I, _I, C.c_float, _P, _P, _P]),
     "spr_ridge_cholesky": (_I, [_P, _P, _I64, _I, C.c_float, C.c_float, _P, _P, _P]),
@@ -53,6 +55,8 @@ PROTOTYPES = {
     "spr_block_sparse_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "spr_block_sparse_attn_workspace_bytes": (_SZ, [_I64, _I64, _I]),
     "spr_block_sparse_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]),
+    "spr_block_sparse_attn_noalloc_status": (_I, [_P]),
+    "spr_selftest_bounded_wait": (_I, [_P, _I, _I64, _P]),
     "spr_sym_eig": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "spr_chol_solve": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "spr_repair_apply": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _I, _P, _P]),

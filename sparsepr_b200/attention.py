@@ -34,6 +34,8 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     batch, heads, tokens, dim = q.shape
     if batch != 1:
         raise RuntimeError("Wan2.2 N8 currently requires batch size one.")
+    if q.is_cuda:
+        K.raise_device_status(q.device)  # the previous layer's status words, if they have landed
     route = core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
                        **route_kw)
     bh = batch * heads
@@ -46,6 +48,7 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     if attn_events is not None:
         attn_events[1].record()
     repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
+    K.collect_status(q.device)
     info["route"] = route
     info["base"] = base
     info["repair_state"] = core.repair_state_current

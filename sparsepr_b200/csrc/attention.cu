@@ -444,6 +444,10 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
 }  // namespace spr
 
+namespace spr {
+static int set_attn_smem_attr();
+}  // namespace spr
+
 using namespace spr;
 
 extern "C" size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq) {
@@ -471,7 +475,7 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
   tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   int s = check_launch("attention tile table");
   if (s) return s;
-  cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+  if ((s = set_attn_smem_attr())) return s;
   // Upper bound on 256-row units per problem: every cluster may add one partial unit.
   const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
   dim3 grid((unsigned)max_tiles, (unsigned)bh);
@@ -493,35 +497,35 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
 //
 // The array is `static __device__`: every GPU that loads this library holds
 // its 256 KiB + 256 B until the process exits.  In host code its name is only
-// a host-side stand-in for the symbol, not a device address, so the host asks
-// the runtime for the real address once per device (cudaGetSymbolAddress with
-// that device current) and passes that pointer to the kernels.
+// a host-side stand-in for the symbol, not a device address, so on every call
+// the host asks the runtime for the real address on the current device
+// (cudaGetSymbolAddress) and passes that pointer to the kernels.  The status
+// word of the last call (0 = ok, else the bounded wait that gave up) is read
+// back with spr_block_sparse_attn_noalloc_status.
 // ---------------------------------------------------------------------------
-#include <mutex>
-
 namespace spr {
 constexpr int kNoAllocStatusInts = 64;       // status word + padding (keeps the table 256-byte aligned)
 constexpr int kNoAllocTableInts = 65536;     // maximum bh * (cq + 1)
-constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) int32_t g_attn_noalloc_scratch[kNoAllocStatusInts + kNoAllocTableInts];
-static std::mutex g_noalloc_mu;
-static int32_t* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
-// Device address of the scratch array on the current device (set up on first use).
+// Device address of the scratch array on the current device, looked up on
+// every call (cheap next to the launches) so that a context created again
+// after cudaDeviceReset never sees a stale address.
 static int noalloc_scratch(int32_t** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "no-alloc attention: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(SPR_ERR_ARG, "no-alloc attention: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(SPR_ERR_LAUNCH, "no-alloc attention: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<int32_t*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(SPR_ERR_LAUNCH, "no-alloc attention: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  *out = static_cast<int32_t*>(p);
+  return SPR_OK;
+}
+
+static int set_attn_smem_attr() {
+  const cudaError_t e =
+      cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+  if (e != cudaSuccess)
+    return fail(SPR_ERR_LAUNCH, "block-sparse attention: shared-memory opt-in (%d B): %s", kSmemTc,
+                cudaGetErrorString(e));
   return SPR_OK;
 }
 }  // namespace spr
@@ -550,7 +554,7 @@ extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_p
   cudaStream_t st = (cudaStream_t)stream;
   tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   if ((s = check_launch("attention tile table"))) return s;
-  cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+  if ((s = set_attn_smem_attr())) return s;
   const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
   dim3 grid((unsigned)max_tiles, (unsigned)bh);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
@@ -558,4 +562,11 @@ extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_p
       (const __nv_bfloat16*)q_perm, (const __nv_bfloat16*)k_perm, (const __nv_bfloat16*)v_perm, q_offsets, k_offsets,
       sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
   return check_launch("block-sparse attention (no-alloc)");
+}
+
+extern "C" int spr_block_sparse_attn_noalloc_status(int* out) {
+  if (!out) return fail(SPR_ERR_ARG, "no-alloc attention status: null output");
+  const cudaError_t e = cudaMemcpyFromSymbol(out, g_attn_noalloc_scratch, sizeof(int32_t));
+  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "no-alloc attention status: %s", cudaGetErrorString(e));
+  return SPR_OK;
 }

@@ -270,3 +270,11 @@ extern "C" int spr_role_projection_status(int* out) {
     return fail(SPR_ERR_LAUNCH, "role projection status: copy failed");
   return SPR_OK;
 }
+
+extern "C" int spr_role_projection_status_async(int32_t* dst, void* stream) {
+  if (!dst) return fail(SPR_ERR_ARG, "role projection status: null destination");
+  const cudaError_t e = cudaMemcpyFromSymbolAsync(dst, g_proj_err, sizeof(int), 0, cudaMemcpyDeviceToDevice,
+                                                  (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "role projection status: %s", cudaGetErrorString(e));
+  return SPR_OK;
+}

@@ -490,6 +490,14 @@ extern "C" int spr_attention_mass_scores_status(int* out) {
   return SPR_OK;
 }
 
+extern "C" int spr_attention_mass_scores_status_async(int32_t* dst, void* stream) {
+  if (!dst) return fail(SPR_ERR_ARG, "attention-mass scores status: null destination");
+  const cudaError_t e = cudaMemcpyFromSymbolAsync(dst, g_scores_err, sizeof(int), 0, cudaMemcpyDeviceToDevice,
+                                                  (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "attention-mass scores status: %s", cudaGetErrorString(e));
+  return SPR_OK;
+}
+
 namespace {
 
 int check_score_shapes(const float* q_centroids, const void* k_sorted, int64_t bh, int cq, int ck, int64_t n, int d,

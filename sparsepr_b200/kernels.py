@@ -300,7 +300,8 @@ def select_budget(scores: torch.Tensor, k_sizes: torch.Tensor, budgets: torch.Te
 
 
 def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
-                           q_order: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                           q_order: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                           _ws_tag: str = "attn") -> torch.Tensor:
     """Block-sparse attention over kept cluster pairs (bf16, d=128) -> [B,Nq,D] bf16."""
     dev = _cuda(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts)
     b, nq, d = q_perm.shape
@@ -314,11 +315,63 @@ def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids
     if out is None:
         out = torch.empty_like(q_perm)
     nbytes = _lib.query("spr_block_sparse_attn_workspace_bytes", b, nq, cq)
-    ws = workspace(dev, nbytes, "attn")
+    ws = workspace(dev, nbytes, _ws_tag)
     _count(2)
     _lib.call("spr_block_sparse_attn", _p(q_perm), _p(k_perm), _p(v_perm), _p(q_offsets), _p(k_offsets), _p(sel_ids),
               _p(sel_counts), b, nq, nk, d, cq, ck, _p(q_order), _p(out), _p(ws), ws.numel(), _stream(dev))
     return out
+
+
+# Per device: (device int32[5] snapshot, pinned host copy, event of the copy).
+_STATUS: dict[tuple, tuple] = {}
+STATUS_WORDS = ("kmeans", "attention", "dense_rows", "role_projection", "attention_mass_scores")
+
+
+def collect_status(dev: torch.device) -> None:
+    """Stream-ordered snapshot of the device status words of the last calls on
+    ``dev`` (k-means, attention, dense probe rows, role projection, scores) into
+    pinned host memory; no synchronisation.  :func:`raise_device_status` reads
+    it once the copy has landed.  Skipped while a CUDA graph is being captured."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    key = (dev.type, dev.index)
+    entry = _STATUS.get(key)
+    if entry is None:
+        entry = (torch.zeros(len(STATUS_WORDS), dtype=torch.int32, device=dev),
+                 torch.zeros(len(STATUS_WORDS), dtype=torch.int32).pin_memory(), torch.cuda.Event())
+        _STATUS[key] = entry
+    buf, host, ev = entry
+    buf.zero_()
+    for i, tag in enumerate(("kmeans", "attn", "attn_dense")):
+        ws = _WS.get((dev.type, dev.index, _SCOPE[0], tag))
+        if ws is not None:
+            buf[i:i + 1].copy_(ws[:4].view(torch.int32))
+    st = _stream(dev)
+    _lib.call("spr_role_projection_status_async", buf[3:4].data_ptr(), st)
+    _lib.call("spr_attention_mass_scores_status_async", buf[4:5].data_ptr(), st)
+    host.copy_(buf, non_blocking=True)
+    ev.record()
+
+
+def raise_device_status(dev: torch.device, wait: bool = False) -> None:
+    """Raise ``RuntimeError`` if the last snapshot of :func:`collect_status` on
+    ``dev`` holds a non-zero status word (a device-side bounded wait gave up, so
+    that call's output is incomplete).  Without ``wait`` a snapshot still in
+    flight is left for a later check."""
+    entry = _STATUS.get((dev.type, dev.index))
+    if entry is None:
+        return
+    _buf, host, ev = entry
+    if wait:
+        ev.synchronize()
+    elif not ev.query():
+        return
+    words = host.tolist()
+    if any(words):
+        bad = {name: w for name, w in zip(STATUS_WORDS, words) if w}
+        host.zero_()
+        raise RuntimeError(f"sparsepr_b200 device status words are non-zero (a bounded device wait gave up; "
+                           f"the output of that call is incomplete): {bad}")
 
 
 def attention_error_code(dev: torch.device) -> int:
@@ -341,7 +394,7 @@ def dense_attention_rows(q_rows: torch.Tensor, k: torch.Tensor, v: torch.Tensor)
     k_off = (two * n).expand(b, 2).contiguous()
     ids = torch.zeros((b, 1, 1), dtype=torch.int32, device=dev)
     cnt = torch.ones((b, 1), dtype=torch.int32, device=dev)
-    return block_sparse_attention(q_rows.contiguous(), k, v, q_off, k_off, ids, cnt)
+    return block_sparse_attention(q_rows.contiguous(), k, v, q_off, k_off, ids, cnt, _ws_tag="attn_dense")
 
 
 def repair_apply(base: torch.Tensor, state, alpha: float, rows: torch.Tensor | None = None,

@@ -10,7 +10,10 @@ the cached cluster-pair lists (already device-resident, so nothing is
 re-planned) and repairs against the current Q/K/V with the cached probe
 rows.
 
-The action for one call (``cosmos_predict2.py:843-859``):
+Steps before ``dense_first_steps`` run exact dense attention and leave the
+cache untouched (``cosmos_predict2.py:1509-1520``); ``RouteCache.action``
+reports them as ``"dense"``.  The action of a sparse call
+(``cosmos_predict2.py:843-859``):
 
 * no cached route                                   -> ``"refresh"``
 * ``share_cfg_route`` and the route was last used in this same step
@@ -97,6 +100,8 @@ class RouteCache:
         return (module_id, 0 if self.config.share_cfg_route else int(branch))
 
     def action(self, module_id, *, step: int, branch: int = 0) -> str:
+        if step < self.config.dense_first_steps:
+            return "dense"
         return route_action(self.entries.get(self.key(module_id, branch)), step=step, config=self.config)
 
     def attention(self, q, k, v, core: N8V6Core, *, module_id, step: int, branch: int = 0,
@@ -106,6 +111,15 @@ class RouteCache:
                                f"{tuple(k.shape)}, {tuple(v.shape)}.")
         batch, heads, tokens, dim = q.shape
         bh = batch * heads
+        if step < self.config.dense_first_steps:
+            # Forced-dense warm-up steps (cosmos_predict2.py:1509-1520): exact
+            # attention, and the route cache is neither read nor written.
+            dt = torch.bfloat16
+            out = K.dense_attention_rows(q.to(dt).contiguous().view(bh, tokens, dim),
+                                         k.to(dt).contiguous().view(bh, tokens, dim),
+                                         v.to(dt).contiguous().view(bh, tokens, dim))
+            self.counts["dense_calls"] = self.counts.get("dense_calls", 0) + 1
+            return out.view(batch, heads, tokens, dim), 1.0, {"route_action": "dense"}
         key = self.key(module_id, branch)
         entry = self.entries.get(key)
         act = route_action(entry, step=step, config=self.config)

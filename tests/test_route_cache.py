@@ -74,3 +74,26 @@ def test_reused_route_attention_matches_oracle():
     got = i2["base"].cpu().view(2, -1, 128)
     torch.testing.assert_close(got.float(), ref.float(), atol=2e-2, rtol=2e-2)
     assert torch.equal(i2["route"].k_sorted_indices, r.k_sorted_indices)
+
+
+@pytest.mark.gpu
+def test_dense_first_steps_run_dense_and_leave_cache():
+    """Steps before dense_first_steps are exact dense attention and do not touch
+    the cache (cosmos_predict2.py:1509-1520); the first sparse step refreshes."""
+    from sparsepr_b200.n8_v6 import N8V6Config, N8V6Core
+    from sparsepr_b200.synthetic import synthetic_qkv
+
+    dev = torch.device("cuda:0")
+    cfg = N8V6Config(num_q_centroids=16, num_k_centroids=24, target_density=0.3, kmeans_iter_init=4,
+                     probe_rows=16, repair_rank=8, role_kv_matmul_precision="highest", kmeans_precision="fp32")
+    core = N8V6Core(cfg)
+    cache = RouteCache(RouteReuseConfig(dense_first_steps=2, route_refresh_every=4))
+    q, k, v = synthetic_qkv(2, 128, (4, 8, 8), dtype=torch.bfloat16)
+    assert cache.action(0, step=0) == "dense"
+    out, density, info = cache.attention(q.to(dev), k.to(dev), v.to(dev), core, module_id=0, step=0)
+    assert info["route_action"] == "dense" and density == 1.0 and not cache.entries
+    assert not core.initialized
+    ref = oracle.dense_attention_rows(q.view(2, -1, 128), k.view(2, -1, 128), v.view(2, -1, 128))
+    torch.testing.assert_close(out.cpu().view(2, -1, 128).float(), ref.float(), atol=2e-2, rtol=2e-2)
+    _, _, i2 = cache.attention(q.to(dev), k.to(dev), v.to(dev), core, module_id=0, step=2)
+    assert i2["route_action"] == "refresh" and cache.counts["dense_calls"] == 1

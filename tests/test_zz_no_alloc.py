@@ -47,6 +47,14 @@ def _noalloc(q, k, v, q_off, k_off, ids, cnt, q_order=None):
     return out
 
 
+def _noalloc_status():
+    import ctypes
+
+    code = ctypes.c_int(-1)
+    _lib.call("spr_block_sparse_attn_noalloc_status", ctypes.addressof(code))
+    return code.value
+
+
 @pytest.mark.parametrize("fused_store", [False, True])
 def test_noalloc_matches_workspace_entry_twice(cuda, fused_store):
     for call, (seed, n, cq, ck) in enumerate([(1, 2000, 13, 50), (2, 1300, 7, 31)]):
@@ -60,6 +68,7 @@ def test_noalloc_matches_workspace_entry_twice(cuda, fused_store):
         ref = K.block_sparse_attention(q, k, v, q_off, k_off, ids, cnt, q_order=order)
         got = _noalloc(q, k, v, q_off, k_off, ids, cnt, order)
         torch.cuda.synchronize()
+        assert _noalloc_status() == 0, call  # no bounded device wait gave up
         err = (got.float() - ref.float()).abs().max().item()
         assert err <= ATOL, (call, err)
         for h in range(bh):
