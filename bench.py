@@ -159,7 +159,7 @@ def run_b200(args):
     from sparsepr_b200.attention import kept_flops
     from sparsepr_b200.graph import GraphedSparseAttention, StreamedSparseAttention
     from sparsepr_b200.sharding import head_shard, reduce_step_stats
-    from sparsepr_b200.synthetic import synthetic_qkv
+    from sparsepr_b200.synthetic import random_init_indices, synthetic_qkv_heads
 
     world, rank, local = _dist()
     if world > 1:
@@ -177,13 +177,16 @@ def run_b200(args):
     local_heads = h1 - h0
     grid = cfgd["grid"]
     n = grid[0] * grid[1] * grid[2]
-    # Synthetic Q/K/V for this rank's heads, generated on the device (seeded per rank).
-    seeds = (1000 * rank, 1000 * rank + 1, 1000 * rank + 2)
-    q, k, v = synthetic_qkv(local_heads, 128, grid, dtype=torch.bfloat16, device=dev, seeds=seeds)
+    # Synthetic Q/K/V for this rank's heads, generated on the device by global head
+    # index (each head has its own seeded generator), so every N processes the same
+    # tensors; the cold-start centroid rows are this rank's rows of the all-heads draw.
+    q, k, v = synthetic_qkv_heads(h0, h1, 128, grid, dtype=torch.bfloat16, device=dev)
     cfg = N8V6Config(**SPARSE)
+    init_rows = (random_init_indices(heads, n, cfg.num_k_centroids, cfg.kmeans_init_seed)[h0:h1].to(dev),
+                 random_init_indices(heads, n, cfg.num_q_centroids, cfg.kmeans_init_seed + 1)[h0:h1].to(dev))
 
     def step(qq, kk, vv, events=None):
-        core = N8V6Core(cfg)  # cold call: full k-means from the seeded init every step
+        core = N8V6Core(cfg, init_indices=init_rows)  # cold call: full k-means from the seeded init every step
         return sparse_attention(qq, kk, vv, core, attn_events=events)
 
     for _ in range(args.warmup):
@@ -219,8 +222,9 @@ def run_b200(args):
 
     # Timed region: the whole layer captured as one CUDA graph (all kernels of
     # the step, fresh routing every replay), inputs resident in HBM.
-    g = GraphedSparseAttention(q.shape, cfg, dev, warmup=max(1, args.warmup)).capture()
-    g.load(q, k, v)
+    g = GraphedSparseAttention(q.shape, cfg, dev, warmup=max(1, args.warmup))
+    g.load(q, k, v, init_rows)
+    g.capture()
     for _ in range(args.warmup):
         g.replay()
     if world > 1:
@@ -239,6 +243,7 @@ def run_b200(args):
     # End to end through the public host-buffer API: every step copies this
     # step's pinned host inputs to the device and the output back, streamed in
     # head chunks so the copies of one chunk overlap the compute of another.
+    sample = tuple(t[:, :2].cpu() for t in (q, k, v)) if world == 1 else None
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hout = torch.empty(hq.shape, dtype=torch.bfloat16).pin_memory()
     del q, k, v, g
@@ -250,7 +255,7 @@ def run_b200(args):
         sg(hq, hk, hv, hout)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_steps = max(1, min(args.steps, 3))
+    e_steps = max(1, args.steps)
     if world > 1:
         dist.barrier()
     e0.record()
@@ -300,7 +305,7 @@ def run_b200(args):
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args, heads_sample=2)
+            line["cpu_baseline"] = cpu_baseline(args, heads_sample=2, qkv=sample)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -455,20 +460,96 @@ def _dit_tensors(model):
             yield from walk(val)
 
 
-def cpu_baseline(args, heads_sample: int = 2):
+def run_kmeans(args):
+    """Config 1: standalone batched k-means (the flash_kmeans workload): 40 problems x
+    75,600 points x 128 bf16, K=256, 10 Lloyd iterations from seeded k-means++ centroids,
+    tol=0.  One JSON line (a side bench, not the layer line): ms per 10-iteration run,
+    TFLOP/s with the reference self-bench's count 2*B*N*D*K*iters
+    (``flash_kmeans/kmeans_triton_impl.py:199-261``), and the device time split into
+    the assignment GEMM and the sort + centroid update, each against its roofline."""
+    from sparsepr_b200 import batch_kmeans_Euclid
+    from sparsepr_b200.synthetic import kmeans_plus_plus, synthetic_kmeans_points
+
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local if world > 1 else 0)
+    b, grid, k, iters, d = (args.heads or 40), (21, 45, 80), 256, 10, 128
+    n = grid[0] * grid[1] * grid[2]
+    x = synthetic_kmeans_points(b, d, grid, 256, device=dev, seed=0)
+    init = kmeans_plus_plus(x, k, seed=3)
+    torch.cuda.synchronize(dev)
+
+    def run():
+        return batch_kmeans_Euclid(x, k, max_iters=iters, tol=0.0, init_centroids=init, round_centroids_to_input=True)
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        t0.record()
+        for _ in range(args.steps):
+            labels, cent, sizes, it = run()
+        t1.record()
+        torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    flops = 2.0 * b * n * d * k * iters
+    # Split of one run's device time between the assignment GEMM and the rest
+    # (label sort, centroid update, norms) from the torch profiler: a share, not a bench value.
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        run()
+        torch.cuda.synchronize(dev)
+    times = [(e.key, e.device_time_total) for e in prof.key_averages() if e.device_time_total > 0]
+    total_us = sum(t for _, t in times)
+    assign_us = sum(t for name, t in times if "assign" in name)
+    assign_ms = ms * assign_us / max(total_us, 1e-9)
+    burst, sustained, hbm, src = _peaks()
+    upd_bytes = iters * (x.numel() * 2 + b * n * 4 * 3)  # per iteration: X read once, labels + order
+    line = {"kmeans": {
+        "workload": "standalone batched k-means (config 1)", "problems": b, "points": n, "dim": d, "k": k,
+        "iters": iters, "dtype": "bf16 points, fp32 distances (TF32-exact on bf16 values), bf16 centroids",
+        "ms_per_run": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+        "assign_ms_per_run": assign_ms, "assign_tflops": flops / (assign_ms * 1e-3) / 1e12,
+        "split": "assignment share of one run's device time (torch profiler), applied to ms_per_run",
+        "update_ms_per_run": ms - assign_ms,
+        "update_gbs": upd_bytes / ((ms - assign_ms) * 1e-3) / 1e9, "hbm_peak_gbs": hbm,
+        "bf16_peak_tflops": burst, "peak_source": src, "steps": args.steps, "warmup": args.warmup,
+        "data": "synthetic smooth mixture of 256 Gaussians on 21x45x80, seeded k-means++ init",
+        "clocks": clocks.summary()}}
+    if not args.no_cpu_baseline:
+        import oracle
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        xs, cs = x[:1].cpu(), init[:1].cpu()
+        t = time.perf_counter()
+        oracle.batch_kmeans_euclid(xs, k, 2, 0.0, cs)
+        dt = time.perf_counter() - t
+        line["kmeans"]["cpu_baseline"] = {
+            "value": 2.0 * n * d * k * 2 / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {b} problems, 2 of {iters} iterations, {dt:.1f} s"}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(args, heads_sample: int = 2, qkv=None):
     """The oracle (CPU restatement of the reference algorithm) on a bounded sample:
-    the same layer on ``heads_sample`` of the 40 heads, scaled to kept TFLOP/s."""
+    the same layer on heads 0..``heads_sample``-1 of the bench's own inputs
+    (``qkv``, else generated like them), scaled to kept TFLOP/s."""
     import types
 
     import oracle
-    from sparsepr_b200.synthetic import synthetic_qkv
+    from sparsepr_b200.synthetic import synthetic_qkv_heads
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     cfgd = CONFIGS[args.config]
     grid = cfgd["grid"]
     n = grid[0] * grid[1] * grid[2]
-    q, k, v = synthetic_qkv(heads_sample, 128, grid, dtype=torch.bfloat16, seeds=(11, 12, 13))
+    if qkv is None:  # the GPU arm generates on the device: use the same generator where there is one
+        gen_dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+        qkv = tuple(t.cpu() for t in synthetic_qkv_heads(0, heads_sample, 128, grid, device=gen_dev))
+    q, k, v = (t[:, :heads_sample] for t in qkv)
     oc = types.SimpleNamespace(role_q_rank=64, role_k_rank=48, metric_sample_tokens=2048, repair_alpha=1.0,
                                repair_norm_cap=0.0, svg_ear_top_p=0.85, adaptive_budget_min_density=0.0,
                                adaptive_budget_max_density=1.0, **SPARSE)
@@ -482,22 +563,33 @@ def cpu_baseline(args, heads_sample: int = 2):
 
 
 def run_reference(args):
+    """The reference algorithm's CPU path (the oracle port) on the box's host cores.
+    Each step is one bounded sample: heads 0-1 of the bench's inputs, the whole layer
+    (route, attention, repair); ``ms_per_step`` is that sample's measured time and
+    the 40-head extrapolation is reported beside it."""
     world, rank, _ = _dist()
     if rank != 0:
         return
-    res = []
-    for _ in range(args.warmup + args.steps if args.steps < 3 else args.steps):
-        res.append(cpu_baseline(args, heads_sample=1))
-    v = statistics.median(x["value"] for x in res[-args.steps:])
-    cb = dict(res[-1])
-    cb["value"] = v
     cfgd = CONFIGS[args.config]
+    grid = cfgd["grid"]
+    gen_dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    from sparsepr_b200.synthetic import synthetic_qkv_heads
+
+    qkv = tuple(t.cpu() for t in synthetic_qkv_heads(0, 2, 128, grid, device=gen_dev))
+    res = [cpu_baseline(args, heads_sample=2, qkv=qkv) for _ in range(args.warmup + args.steps)]
+    timed = res[args.warmup:]
+    v = statistics.median(x["value"] for x in timed)
+    cb = dict(timed[-1])
+    cb["value"] = v
+    sample_ms = statistics.median(x["seconds"] for x in timed) * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": cb["ms_per_layer_extrapolated"], "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": sample_ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32 (CPU)", "data": "synthetic",
+        "step": "one bounded sample: 2 of the 40 heads, full layer",
+        "ms_per_layer_extrapolated": sample_ms * cfgd["heads"] / 2,
         "config": {"workload": cfgd["name"], "tokens": cfgd["grid"][0] * cfgd["grid"][1] * cfgd["grid"][2],
-                   "heads": cfgd["heads"], "sample_heads": 1},
+                   "heads": cfgd["heads"], "sample_heads": 2},
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -510,8 +602,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS) + [4],
-                    help="3 (default) or 2: the SparsePR layer; 4: a HunyuanVideo-architecture DiT step")
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS) + [1, 4],
+                    help="3 (default) or 2: the SparsePR layer; 1: standalone batched k-means; "
+                         "4: a HunyuanVideo-architecture DiT step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
@@ -529,6 +622,8 @@ def main():
         run_ulysses(args)
     elif args.config == 4:
         run_dit(args)
+    elif args.config == 1:
+        run_kmeans(args)
     else:
         run_b200(args)
 

@@ -46,6 +46,7 @@ __all__ = [
     "random_init_indices",
     "OracleRoute",
     "oracle_route",
+    "OracleCore",
     "oracle_repair",
     "oracle_sparse_attention",
     "kept_pairs",
@@ -583,6 +584,102 @@ def oracle_route(q, k, v, cfg, *, k_init=None, q_init=None, init_seed: int = 0,
     routed = select_budget(scores, k_sizes, budgets)
     return OracleRoute(q_labels, k_labels, q_sizes, k_sizes, routed[:, 1:, 1:], qfeat, kfeat,
                        q_cent, k_cent, v_cent, k_order, q_order, k_perm, v_perm, scores, budgets, q_it, k_it)
+
+
+class OracleCore:
+    """Stateful ``N8V6Core.route`` across calls (``models/common/n8_v6.py:372-1172``),
+    symmetric heads (no GQA), no text suffix, ``factor_refresh_every = 1``.
+
+    The first call is :func:`oracle_route` (cold start, ``kmeans_iter_init``
+    iterations from the rows at ``random_init_indices``).  Later calls are the
+    reference's warm path:
+
+    * role factors by warm subspace iteration from the previous bases
+      (``n8_v6.py:478-519`` -> ``operator_kmeans.py:221-477``), a head whose
+      warm solve fails keeping its previous factor and basis;
+    * K initial centroids = previous original-space K centroids projected by
+      the new K factor and divided by the new K feature scale
+      (``n8_v6.py:686-697``); Q initial centroids = previous Q centroids
+      projected by the new Q factor, row-RMS normalised (``n8_v6.py:779-783``);
+    * ``kmeans_iter_step`` Lloyd iterations for both (``n8_v6.py:698``) with the
+      k-means ``tol``;
+    * original-space centroids with empty clusters keeping the previous ones
+      (``n8_v6.py:734-741, 796``).
+    """
+
+    def __init__(self, cfg, *, init_seed: int = 0, tol: float = 1e-4):
+        self.cfg = cfg
+        self.init_seed = int(init_seed)
+        self.tol = float(tol)
+        self.state = None
+
+    def route(self, q, k, v) -> OracleRoute:
+        if self.state is None:
+            r, self.state = _route(q, k, v, self.cfg, None, init_seed=self.init_seed, tol=self.tol)
+        else:
+            r, self.state = _route(q, k, v, self.cfg, self.state, tol=self.tol)
+        return r
+
+
+def _route(q, k, v, cfg, prev, *, init_seed: int = 0, tol: float = 0.0):
+    """One call of :class:`OracleCore`: cold when ``prev`` is None, else warm from
+    ``prev`` (dict of the previous call's centroids and factor states)."""
+    b, h, n, d = q.shape
+    bh = b * h
+    q3, k3, v3 = (t.reshape(bh, n, d) for t in (q, k, v))
+    if prev is None:
+        r = oracle_route(q, k, v, cfg, init_seed=init_seed, tol=tol)
+        kf = metric_factor(key_metric_from_queries(q3, cfg.metric_sample_tokens), cfg.role_k_rank)
+        qf = metric_factor(query_metric_from_key_centroids(r.k_centroids, r.k_sizes), cfg.role_q_rank)
+        return r, {"k_centroids": r.k_centroids, "v_centroids": r.v_centroids, "q_centroids": r.q_centroids,
+                   "k_factor": kf, "k_basis": kf, "q_factor": qf, "q_basis": qf}
+    warm = dict(power_iters=getattr(cfg, "factor_power_iters", 2),
+                rayleigh_ridge=getattr(cfg, "factor_rayleigh_ridge", 1e-4),
+                cholesky_qr_ridge=getattr(cfg, "factor_cholesky_qr_ridge", 1e-5))
+
+    def updated(metric, basis, current, rank):
+        f, st, bad = warm_subspace_metric_factor(metric, basis, rank, **warm)
+        sel = bad[:, None, None]
+        return torch.where(sel, current, f), torch.where(sel, basis, st)
+
+    k_factor, k_basis = updated(key_metric_from_queries(q3, cfg.metric_sample_tokens), prev["k_basis"],
+                                prev["k_factor"], cfg.role_k_rank)
+    kfeat = torch.bmm(k3.float(), k_factor)
+    kscale = kfeat.square().mean(dim=(1, 2), keepdim=True).sqrt().clamp_min(1e-8)
+    kfeat = kfeat / kscale
+    k_init = torch.bmm(prev["k_centroids"], k_factor) / kscale
+    iters = cfg.kmeans_iter_step
+    k_labels, _, k_sizes, k_it = batch_kmeans_euclid(kfeat, cfg.num_k_centroids, iters, tol, k_init)
+    k_cent = original_centroids(k3, k_labels, k_sizes, prev["k_centroids"])
+    v_cent = original_centroids(v3, k_labels, k_sizes, prev["v_centroids"])
+    q_factor, q_basis = updated(query_metric_from_key_centroids(k_cent, k_sizes), prev["q_basis"],
+                                prev["q_factor"], cfg.role_q_rank)
+    qfeat = torch.bmm(q3.float(), q_factor)
+    qfeat = qfeat / qfeat.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)
+    qi = torch.bmm(prev["q_centroids"], q_factor)
+    q_init = qi / qi.square().mean(dim=2, keepdim=True).sqrt().clamp_min(1e-6)
+    q_labels, _, q_sizes, q_it = batch_kmeans_euclid(qfeat, cfg.num_q_centroids, iters, tol, q_init)
+    q_cent = original_centroids(q3, q_labels, q_sizes, prev["q_centroids"])
+    k_order = stable_label_order(k_labels)
+    q_order = stable_label_order(q_labels)
+    k_perm = permute_rows(k3, k_order)
+    v_perm = permute_rows(v3, k_order)
+    if getattr(cfg, "selector_policy", "attention_mass") == "svg_ear_value":
+        scores = svg_ear_value_error_scores(q_cent, k_perm, v_perm, k_cent, v_cent, k_sizes)
+    else:
+        scores = attention_mass_scores(q_cent, k_perm, k_sizes)
+    if cfg.selector_budget_mode == "fixed_density":
+        budget = fixed_density_budget(cfg.target_density, cfg.probe_rows, n, n, 0)
+        budgets = torch.full((bh, cfg.num_q_centroids), budget, dtype=torch.long)
+    else:
+        budgets = svg_top_p_key_budgets(q_cent, k_cent, k_sizes, cfg.svg_ear_top_p)
+        budgets = budgets.clamp(min=int(math.ceil(cfg.adaptive_budget_min_density * n)),
+                                max=int(math.floor(cfg.adaptive_budget_max_density * n)))
+    routed = select_budget(scores, k_sizes, budgets)
+    r = OracleRoute(q_labels, k_labels, q_sizes, k_sizes, routed[:, 1:, 1:], qfeat, kfeat,
+                    q_cent, k_cent, v_cent, k_order, q_order, k_perm, v_perm, scores, budgets, q_it, k_it)
+    return r, {"k_centroids": k_cent, "v_centroids": v_cent, "q_centroids": q_cent,
+               "k_factor": k_factor, "k_basis": k_basis, "q_factor": q_factor, "q_basis": q_basis}
 
 
 def oracle_repair(base, q, k, v, route, cfg):

@@ -52,7 +52,10 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     info["route"] = route
     info["base"] = base
     info["repair_state"] = core.repair_state_current
-    return repaired, float(info["effective_video_density"]), info
+    density = info["effective_video_density"]
+    if isinstance(density, torch.Tensor) and not torch.cuda.is_current_stream_capturing():
+        density = float(density)  # top-p budgets: the one host read of the layer, as in the reference
+    return repaired, density, info
 
 
 def hunyuan_attend(query, key, value, core: N8V6Core, *, video_tokens: int, prompt_length: int):

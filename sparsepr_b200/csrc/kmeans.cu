@@ -253,6 +253,7 @@ struct KmeansWs {
   int32_t* counts;   // per-(cluster, chunk) counts / starts of the label sort
   float* next;       // updated centroids
   float* caug;       // augmented centroid rows of the folded-bias assignment (may be empty)
+  __nv_bfloat16* cbf;  // bf16 centroid operands of the bf16 assignment path
 };
 
 static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
@@ -269,6 +270,7 @@ static KmeansWs carve_kmeans(Carver& c, int64_t bh, int64_t n, int d, int k) {
   w.next = c.take<float>((size_t)bh * k * d);
   const size_t naug = d > 0 ? centroid_aug_count(bh, d, k) : 0;
   w.caug = naug ? c.take<float>(naug) : nullptr;
+  w.cbf = d > 0 ? c.take<__nv_bfloat16>((size_t)bh * k * d) : nullptr;
   return w;
 }
 
@@ -395,9 +397,14 @@ extern "C" int spr_kmeans_lloyd(const void* x, int x_dtype, int64_t bh, int64_t 
   cudaMemsetAsync(w.err, 0, (size_t)((char*)(w.shifts + 1024) - (char*)w.err), st);
   cudaMemsetAsync(iters_done, 0, sizeof(int32_t), st);
   const int64_t count = bh * k * (int64_t)d;
-  if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st))) return s;
+  // bf16 points whose centroids are rounded to bf16 after every update (the
+  // standalone flash_kmeans contract): bf16 tensor-core distances.
+  const bool cbf_ok = x_dtype == SPR_BF16 && centroid_round_dtype == SPR_BF16 && d % 8 == 0;
+  if ((s = launch_point_sq(x, x_dtype, precision, bh, n, d, w.xsq, w.xmax, st, cbf_ok))) return s;
   for (int it = 0; it < iters; ++it) {
-    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, w.caug, precision, labels, done, w.err, st))) return s;
+    if ((s = launch_assign(x, x_dtype, bh, n, d, k, centroids, w.xsq, w.xmax, w.csq, w.bias, w.caug, precision, labels,
+                           done, w.err, st, cbf_ok ? w.cbf : nullptr)))
+      return s;
     if ((s = launch_label_sort(labels, bh, n, k, sizes, offsets, order, counts, done, st))) return s;
     if ((s = seg_mean_dispatch(x_dtype, x, order, offsets, bh, n, d, k, centroids, next, nullptr, 1,
                                centroid_round_dtype, shifts + it, done, st)))

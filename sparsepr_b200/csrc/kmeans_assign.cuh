@@ -30,6 +30,7 @@ constexpr int kAsgThreads = 416;
 constexpr int kAsgLoaders = 128;
 constexpr int kAsgEpilogue = 256;
 constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
+constexpr uint32_t kIdescAsgBf = tc::idesc_bf16_f32(128, 128, 0);  // both operands K-major
 
 template <int DP, bool SPLIT>
 struct AsgSmem {
@@ -445,11 +446,18 @@ inline int fold_row(int d) { return fold_head(d) + 8; }
 template <int DP>
 inline bool assign_folds(int d) { return fold_row(d) <= DP; }
 
-template <int DP, bool FOLD = false>
+// BF: bf16 points and bf16 centroid operands, kind::f16 MMAs (the standalone
+// flash_kmeans path, whose centroids are rounded to the input dtype); else
+// fp32 operands at TF32.  Both use 32-byte MMA K steps over 128-byte
+// swizzled row blocks (8 tf32 or 16 bf16 features per step).
+template <int DP, bool FOLD = false, bool BF = false>
 struct TmaAsg {
-  static constexpr int kMT = DP <= 64 ? 2 : 1;   // 128-point M tiles per item
-  static constexpr int kBlocks = DP / 32;         // 128-byte column blocks per row
-  static constexpr int kTileBytes = 128 * DP * 4; // one 128-row tile of points or centroids
+  static constexpr int kElem = BF ? 2 : 4;
+  static constexpr int kRowBytes = DP * kElem;
+  static constexpr int kMT = kRowBytes <= 256 ? 2 : 1;  // 128-point M tiles per item
+  static constexpr int kBlocks = kRowBytes / 128;       // 128-byte column blocks per row
+  static constexpr int kBlockElems = 128 / kElem;       // features per 128-byte block
+  static constexpr int kTileBytes = 128 * kRowBytes;    // one 128-row tile of points or centroids
   static constexpr int kXBytes = kMT * kTileBytes;
   static constexpr int kOnesBytes = FOLD ? 128 * 128 : 0;  // all-ones A tile (128 rows x 128 bytes)
   static constexpr int kBudget = 216 * 1024 - kOnesBytes;
@@ -463,15 +471,16 @@ struct TmaAsg {
 };
 
 // max over the points of problem b of |x|^2 into xmax[b] (zeroed by the caller).
-__global__ void point_sqmax_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ xmax) {
+template <typename T>
+__global__ void point_sqmax_kernel(const T* __restrict__ x, int64_t n, int d, float* __restrict__ xmax) {
   __shared__ float s_max[8];
   const int64_t b = blockIdx.y;
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   float s = 0.f;
   if (p < n) {
-    const float4* r = reinterpret_cast<const float4*>(x + (b * n + p) * d);
+    const T* r = x + (b * n + p) * d;
     for (int e = 0; e < d / 4; ++e) {
-      const float4 v = r[e];
+      const float4 v = load4<T>(r + 4 * e);
       s = fmaf(v.x, v.x, s);
       s = fmaf(v.y, v.y, s);
       s = fmaf(v.z, v.z, s);
@@ -503,11 +512,14 @@ __global__ void point_sqmax_kernel(const float* __restrict__ x, int64_t n, int d
 // With caug (folded bias), row i of caug[b] ([k][fold_row(d)]) becomes
 // [-2c_i | 0 | hi_i, lo_i, 0 x 6], hi_i = tf32(|c_i|^2 + B) (low 13 bits
 // cleared) and lo_i = |c_i|^2 + B - hi_i; the last block writes hi and lo.
+//
+// With cbf (the bf16 path), the centroids are rounded to bf16 into cbf[b][k][d]
+// and |c|^2 is taken of the rounded values (the MMA operand itself).
 __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restrict__ c, int k, int d, int kpad,
                                                             const float* __restrict__ xmax, float* __restrict__ csqb,
                                                             float* __restrict__ bias, float* __restrict__ cmax,
                                                             unsigned* __restrict__ count, const int* __restrict__ done,
-                                                            float* __restrict__ caug) {
+                                                            float* __restrict__ caug, __nv_bfloat16* __restrict__ cbf) {
   if (done && *done) return;
   __shared__ float s_max[4];
   __shared__ bool s_last;
@@ -518,7 +530,15 @@ __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restr
   if (i < k) {
     const float4* r = reinterpret_cast<const float4*>(c + (b * k + i) * d);
     for (int e = 0; e < d / 4; ++e) {
-      const float4 v = r[e];
+      float4 v = r[e];
+      if (cbf) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        v = make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&lo);
+        u.y = *reinterpret_cast<const uint32_t*>(&hi);
+        reinterpret_cast<uint2*>(cbf + (b * k + i) * d)[e] = u;
+      }
       s = fmaf(v.x, v.x, s);
       s = fmaf(v.y, v.y, s);
       s = fmaf(v.z, v.z, s);
@@ -570,12 +590,13 @@ __global__ void __launch_bounds__(128) centroid_bias_kernel(const float* __restr
   }
 }
 
-template <int DP, bool FOLD>
+template <int DP, bool FOLD, bool BF>
 __global__ void __launch_bounds__(kTmaAsgThreads, 1)
 assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap, int64_t n,
                   int d, int k, int64_t items, const float* __restrict__ csqb, const float* __restrict__ bias,
                   int32_t* __restrict__ labels, const int* __restrict__ done, int* __restrict__ err) {
-  using L = TmaAsg<DP, FOLD>;
+  using L = TmaAsg<DP, FOLD, BF>;
+  static_assert(!(FOLD && BF), "the folded bias is a TF32-path option");
   constexpr int MT = L::kMT, NX = L::kNX, NC = L::kNC, NQ = L::kNQ, CG = L::kCG;
   constexpr int kBlocksPerThread = 4 / CG;  // 32-column TMEM blocks scanned per tile
   if (done && *done) return;
@@ -652,8 +673,8 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
         for (int mt = 0; mt < mts; ++mt)
 #pragma unroll
           for (int j = 0; j < L::kBlocks; ++j)
-            tc::tma_load_3d(xbase + mt * L::kTileBytes + j * (kAsgM * 128), &xmap, 32 * j, (int)(p0 + mt * kAsgM), b,
-                            &bar_x_full[xb]);
+            tc::tma_load_3d(xbase + mt * L::kTileBytes + j * (kAsgM * 128), &xmap, L::kBlockElems * j,
+                            (int)(p0 + mt * kAsgM), b, &bar_x_full[xb]);
         ++nx;
         for (int t = 0; t < ctiles; ++t) {
           const int st = (int)(nc % NC), q = (int)(nc % NQ);
@@ -664,7 +685,7 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
           tc::mbar_expect_tx(&bar_c_full[st], (uint32_t)L::kTileBytes);
 #pragma unroll
           for (int j = 0; j < L::kBlocks; ++j)
-            tc::tma_load_3d(cbase + j * (kAsgN * 128), &cmap, 32 * j, t * kAsgN, b, &bar_c_full[st]);
+            tc::tma_load_3d(cbase + j * (kAsgN * 128), &cmap, L::kBlockElems * j, t * kAsgN, b, &bar_c_full[st]);
           if constexpr (!FOLD) {
             tc::mbar_expect_tx(&bar_q_full[q], kAsgN * 4);
             tc::bulk_load(tc::smem_addr(&s_csq[q][0]), csqb + ((int64_t)b * ctiles + t) * kAsgN, kAsgN * 4,
@@ -685,7 +706,7 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
   } else if (warp == 8) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const int ksteps = (d + 7) / 8;
+      const int ksteps = BF ? (d + 15) / 16 : (d + 7) / 8;  // 32-byte K steps
       // FOLD: the K step over features [dh, dh + 8) of the centroid row (hi, lo, zeros) against ones.
       const uint32_t kbf = (uint32_t)ksteps * 32;
       const uint32_t offf = (kbf >> 7) * (kAsgN * 128) + (kbf & 127);
@@ -709,13 +730,17 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
             if constexpr (FOLD)
               tc::mma_tf32(dt, tc::sw128_desc(sones, 16, 1024), tc::sw128_desc(cbase + offf, 16, 1024), kIdescAsg,
                            false);
-            // 8 tf32 (32 bytes) per MMA K step; steps wholly inside the zero
-            // padding past d are skipped.
+            // 8 tf32 or 16 bf16 (32 bytes) per MMA K step; steps wholly inside
+            // the zero padding past d are skipped.
             for (int kk = 0; kk < ksteps; ++kk) {
               const uint32_t kb = kk * 32;
               const uint32_t off = (kb >> 7) * (kAsgM * 128) + (kb & 127);
-              tc::mma_tf32(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
-                           tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, FOLD || kk > 0);
+              if constexpr (BF)
+                tc::mma_f16(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
+                            tc::sw128_desc(cbase + off, 16, 1024), kIdescAsgBf, kk > 0);
+              else
+                tc::mma_tf32(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
+                             tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, FOLD || kk > 0);
             }
           }
           tc::mma_commit(&bar_d_full[db]);
@@ -746,12 +771,23 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
       if (ok) {
         const uint8_t* xt = smem + xb * L::kXBytes + mt * L::kTileBytes;
 #pragma unroll
-        for (int ch = 0; ch < DP / 4; ++ch) {
-          const float4 v = *reinterpret_cast<const float4*>(xt + tc::sw128_off(row, ch, kAsgM));
-          xsq = fmaf(v.x, v.x, xsq);
-          xsq = fmaf(v.y, v.y, xsq);
-          xsq = fmaf(v.z, v.z, xsq);
-          xsq = fmaf(v.w, v.w, xsq);
+        for (int ch = 0; ch < L::kRowBytes / 16; ++ch) {
+          if constexpr (BF) {
+            const uint4 u = *reinterpret_cast<const uint4*>(xt + tc::sw128_off(row, ch, kAsgM));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
+              xsq = fmaf(__low2float(h), __low2float(h), xsq);
+              xsq = fmaf(__high2float(h), __high2float(h), xsq);
+            }
+          } else {
+            const float4 v = *reinterpret_cast<const float4*>(xt + tc::sw128_off(row, ch, kAsgM));
+            xsq = fmaf(v.x, v.x, xsq);
+            xsq = fmaf(v.y, v.y, xsq);
+            xsq = fmaf(v.z, v.z, xsq);
+            xsq = fmaf(v.w, v.w, xsq);
+          }
         }
       }
       tc::mbar_arrive(&bar_x_read[xb]);
@@ -877,23 +913,28 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
   }
 }
 
-// 3-D map over [bh][rows][d] fp32 rows: box 32 features x 128 rows x 1, 128-byte swizzle.
-inline int encode_row_map(CUtensorMap* m, const float* base, int d, int64_t rows, int64_t bh, const char* what) {
-  return encode_map_3d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, d, rows, bh, 32, kAsgM, what);
+// 3-D map over [bh][rows][d] rows: box of one 128-byte block (32 fp32 or 64 bf16
+// features) x 128 rows x 1, 128-byte swizzle.
+inline int encode_row_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t rows, int64_t bh,
+                          const char* what) {
+  return bf16 ? encode_map_3d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, d, rows, bh, 64, kAsgM, what)
+              : encode_map_3d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, d, rows, bh, 32, kAsgM, what);
 }
 
-template <int DP, bool FOLD>
-static int launch_assign_tma_as(const float* x, int64_t bh, int64_t n, int d, int k, const float* c,
+template <int DP, bool FOLD, bool BF = false>
+static int launch_assign_tma_as(const void* x, int64_t bh, int64_t n, int d, int k, const void* c,
                                 const float* csqb, const float* bias, int32_t* labels, const int* done, int* err,
                                 cudaStream_t st) {
-  using L = TmaAsg<DP, FOLD>;
+  using L = TmaAsg<DP, FOLD, BF>;
   CUtensorMap xmap, cmap;
-  int s = encode_row_map(&xmap, x, d, n, bh, "points");
-  // FOLD: c is the augmented centroid array [bh][k][fold_row(d)].
-  if (!s) s = encode_row_map(&cmap, c, FOLD ? fold_row(d) : d, k, bh, "centroids");
+  int s = encode_row_map(&xmap, x, BF, d, n, bh, "points");
+  // FOLD: c is the augmented centroid array [bh][k][fold_row(d)]; BF: the bf16 centroid copy.
+  if (!s) s = encode_row_map(&cmap, c, BF, FOLD ? fold_row(d) : d, k, bh, "centroids");
   if (s) return s;
-  auto kern = assign_tma_kernel<DP, FOLD>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  auto kern = assign_tma_kernel<DP, FOLD, BF>;
+  const cudaError_t ae = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (ae != cudaSuccess)
+    return fail(SPR_ERR_LAUNCH, "k-means assign: shared-memory opt-in (%d B): %s", L::kTotal, cudaGetErrorString(ae));
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -925,19 +966,27 @@ inline size_t centroid_aug_count(int64_t bh, int d, int k) {
 // Padded |c|^2 entries needed by the TMA path: [bh][128 * centroid tiles].
 inline size_t centroid_sq_pad_count(int64_t bh, int k) { return (size_t)bh * (size_t)((k + kAsgN - 1) / kAsgN) * kAsgN; }
 
-// The TMA path serves fp32 points at TF32 precision; other cases use the
-// register-staged kernel above.
-inline bool assign_uses_tma(int x_dtype, int precision) { return x_dtype == SPR_F32 && precision == SPR_KMEANS_TF32; }
+// The TMA path serves fp32 points at TF32 precision, and bf16 points when the
+// caller keeps its centroids in bf16 (cbf_ok: the standalone flash_kmeans
+// path rounds every update to the input dtype, so bf16 MMAs see the exact
+// centroids); other cases use the register-staged kernel above.
+inline bool assign_uses_tma(int x_dtype, int precision, bool cbf_ok = false) {
+  return precision == SPR_KMEANS_TF32 && (x_dtype == SPR_F32 || (x_dtype == SPR_BF16 && cbf_ok));
+}
 
 // Per-run point statistics (call once per k-means run: x does not change):
 // |x|^2 per point for the register path, max |x|^2 per problem for the TMA
 // path (which computes |x|^2 itself).
 inline int launch_point_sq(const void* x, int x_dtype, int precision, int64_t bh, int64_t n, int d, float* xsq,
-                           float* xmax, cudaStream_t st) {
-  if (assign_uses_tma(x_dtype, precision)) {
+                           float* xmax, cudaStream_t st, bool cbf_ok = false) {
+  if (assign_uses_tma(x_dtype, precision, cbf_ok)) {
     // xmax and the bias scratch that follows it (4 * bh words) start at 0.
     cudaMemsetAsync(xmax, 0, (size_t)bh * 5 * sizeof(float), st);
-    point_sqmax_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)bh), 256, 0, st>>>((const float*)x, n, d, xmax);
+    const dim3 grid((unsigned)((n + 255) / 256), (unsigned)bh);
+    if (x_dtype == SPR_BF16)
+      point_sqmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, n, d, xmax);
+    else
+      point_sqmax_kernel<float><<<grid, 256, 0, st>>>((const float*)x, n, d, xmax);
     return check_launch("point norm maxima");
   }
   if (x_dtype != SPR_F32) return SPR_OK;  // other dtypes compute |x|^2 inside the assignment kernel
@@ -952,16 +1001,24 @@ inline int launch_point_sq(const void* x, int x_dtype, int precision, int64_t bh
 // centroid_bias_kernel (zeroed once per run by launch_point_sq).
 // caug: augmented centroid rows for the folded-bias TMA path
 // (centroid_aug_count floats; nullptr when that count is 0).
+// cbf: bf16 centroid scratch [bh][k][d] for the bf16 TMA path (cbf_ok).
 inline int launch_assign(const void* x, int x_dtype, int64_t bh, int64_t n, int d, int k, const float* c,
                          const float* xsq, const float* xmax, float* csq, float* bias, float* caug, int precision,
-                         int32_t* labels, const int* done, int* err, cudaStream_t st) {
-  if (assign_uses_tma(x_dtype, precision)) {
+                         int32_t* labels, const int* done, int* err, cudaStream_t st, __nv_bfloat16* cbf = nullptr) {
+  const bool cbf_ok = cbf != nullptr;
+  if (assign_uses_tma(x_dtype, precision, cbf_ok)) {
     const int kpad = (k + kAsgN - 1) / kAsgN * kAsgN;
-    if (!assign_fold_for(d)) caug = nullptr;
+    const bool bf = x_dtype == SPR_BF16;
+    if (!assign_fold_for(d) || bf) caug = nullptr;
     centroid_bias_kernel<<<dim3((unsigned)(kpad / kAsgN), (unsigned)bh), 128, 0, st>>>(
-        c, k, d, kpad, xmax, csq, bias, bias + 2 * bh, reinterpret_cast<unsigned*>(bias + 3 * bh), done, caug);
+        c, k, d, kpad, xmax, csq, bias, bias + 2 * bh, reinterpret_cast<unsigned*>(bias + 3 * bh), done, caug,
+        bf ? cbf : nullptr);
     int s = check_launch("centroid norms");
     if (s) return s;
+    if (bf) {
+      if (d <= 64) return launch_assign_tma_as<64, false, true>(x, bh, n, d, k, cbf, csq, bias, labels, done, err, st);
+      return launch_assign_tma_as<128, false, true>(x, bh, n, d, k, cbf, csq, bias, labels, done, err, st);
+    }
     const float* xf = (const float*)x;
     if (d <= 32) return launch_assign_tma<32>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);
     if (d <= 64) return launch_assign_tma<64>(xf, bh, n, d, k, c, caug, csq, bias, labels, done, err, st);

@@ -2,7 +2,7 @@
 end that streams a layer through captured graphs in head chunks.
 
 Every step of ``sparse_attention`` is stream-ordered device work with no host
-synchronisation (fixed-density budgets), so a whole layer — role factors,
+synchronisation (the top-p budget density stays on the device), so a whole layer — role factors,
 both k-means runs, permutes, scores, selection, block-sparse attention, dense
 probes, fit and repair — can be captured once and replayed with a single
 launch.  Inputs are copied into static device buffers before each replay.
@@ -29,15 +29,13 @@ class GraphedSparseAttention:
 
     Each replay routes from scratch (a fresh core per call, like the first
     denoising step), so replays are independent of each other.
-    ``selector_budget_mode`` must be ``fixed_density`` (the top-p mode reads
-    its density on the host).  The graph's kernels use workspaces private to
+    With ``svg_ear_top_p`` budgets ``density`` is a 0-dim device tensor
+    updated by every replay.  The graph's kernels use workspaces private to
     this object, so different graphs may replay concurrently on different
     streams.
     """
 
     def __init__(self, shape, config: N8V6Config, device: torch.device, warmup: int = 2):
-        if config.selector_budget_mode != "fixed_density":
-            raise ValueError("graph capture needs selector_budget_mode='fixed_density'")
         self.config = config
         self.device = device
         self.q = torch.zeros(shape, dtype=torch.bfloat16, device=device)

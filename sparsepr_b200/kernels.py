@@ -359,7 +359,7 @@ def raise_device_status(dev: torch.device, wait: bool = False) -> None:
     that call's output is incomplete).  Without ``wait`` a snapshot still in
     flight is left for a later check."""
     entry = _STATUS.get((dev.type, dev.index))
-    if entry is None:
+    if entry is None or torch.cuda.is_current_stream_capturing():
         return
     _buf, host, ev = entry
     if wait:

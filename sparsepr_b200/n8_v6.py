@@ -367,6 +367,12 @@ def select_first_token_largest_groups(role_features, role_labels, num_clusters: 
     return sel, ssz / ssz.mean(dim=1, keepdim=True).clamp_min(1e-20)
 
 
+def _clamp_density(d):
+    """min(1, d) for a float or a 0-dim device tensor (top-p budgets keep the
+    density on the device)."""
+    return d.clamp(max=1.0) if isinstance(d, torch.Tensor) else min(1.0, d)
+
+
 def fit_reduced_rank_residual(x_fit, y_fit, weights, rank: int, ridge: float):
     """Weighted ridge RRR, dual Cholesky, raw-residual basis (``residual_repair.py:317-465``).
 
@@ -671,7 +677,9 @@ class N8V6Core:
             budgets = budgets.clamp(min=int(math.ceil(cfg.adaptive_budget_min_density * tokens)),
                                     max=int(math.floor(cfg.adaptive_budget_max_density * tokens))).to(torch.int32)
             pair = (budgets.long() * q_sizes.long()).sum(dim=1).float() / float(tokens * tokens)
-            base_density = float(pair.mean().item())
+            # A 0-dim device tensor: read on the host only when the caller asks
+            # (the reference synchronises here, n8_v6.py:1057-1060).
+            base_density = pair.mean()
         routed, sel_ids, sel_counts = K.select_budget(scores, k_sizes, budgets)
         route = N8V6Route(
             q_labels=q_labels, k_labels=k_labels, q_cluster_sizes=q_sizes, k_cluster_sizes=k_sizes,
@@ -731,6 +739,6 @@ class N8V6Core:
             "repair_basis_source": cfg.repair_basis_source,
             "repair_backend": "sparsepr_b200",
             "repair_recovery_policy": policy,
-            "effective_video_density": min(1.0, route.base_video_density + count / float(tokens)),
+            "effective_video_density": _clamp_density(route.base_video_density + count / float(tokens)),
         }
         return corrected.view(batch, heads, tokens, dim), info

@@ -15,6 +15,7 @@ __all__ = [
     "gaussian_blur_matrix",
     "smooth_field",
     "synthetic_qkv",
+    "synthetic_qkv_heads",
     "synthetic_kmeans_points",
     "kmeans_plus_plus",
     "random_init_indices",
@@ -59,6 +60,32 @@ def synthetic_qkv(heads: int, head_dim: int, grid: tuple[int, int, int], *, batc
             x = x + noise * torch.randn(x.shape, generator=g, device=device)
         x = x.view(batch, heads, head_dim, n).transpose(2, 3).contiguous()
         out.append(x.to(dtype))
+    return tuple(out)
+
+
+def synthetic_qkv_heads(h0: int, h1: int, head_dim: int, grid: tuple[int, int, int], *, sigma: float = 2.0,
+                        noise: float = 0.5, dtype=torch.bfloat16, device=None, seeds=(0, 1, 2)):
+    """Heads ``[h0, h1)`` of a per-head-seeded Q/K/V set, each [1, h1-h0, N, D].
+
+    Head ``h`` of role ``r`` draws from its own generator (seed
+    ``seeds[r] * 1_000_003 + h``), so any head range (one rank's shard, a CPU
+    sample) equals the same heads of the full set, whatever the sharding.
+    Same statistics as :func:`synthetic_qkv`.
+    """
+    n = grid[0] * grid[1] * grid[2]
+    out = []
+    for role, seed in zip("qkv", seeds):
+        t = torch.empty((1, h1 - h0, n, head_dim), dtype=dtype, device=device)
+        for i, h in enumerate(range(h0, h1)):
+            g = torch.Generator(device=device if device is not None else "cpu").manual_seed(
+                int(seed) * 1_000_003 + int(h))
+            if role == "v":
+                x = torch.randn((head_dim, n), generator=g, device=device)
+            else:
+                x = smooth_field(head_dim, grid, sigma, g, device=device)
+                x = x + noise * torch.randn(x.shape, generator=g, device=device)
+            t[0, i] = x.t().to(dtype)
+        out.append(t)
     return tuple(out)
 
 

@@ -26,7 +26,7 @@ def test_layer_status_words_raise_on_next_call(cuda):
     from sparsepr_b200.synthetic import synthetic_qkv
 
     cfg = N8V6Config(num_q_centroids=16, num_k_centroids=24, target_density=0.3, kmeans_iter_init=3,
-                     probe_rows=16, repair_rank=8, selector_policy="attention_mass",
+                     probe_rows=16, repair_rank=16, selector_policy="attention_mass",
                      role_kv_matmul_precision="highest", kmeans_precision="fp32")
     q, k, v = (t.to(cuda) for t in synthetic_qkv(2, 128, (4, 8, 8), dtype=torch.bfloat16))
     sparse_attention(q, k, v, N8V6Core(cfg))

@@ -180,3 +180,37 @@ def test_svg_value_route_matches_reference():
     assert torch.equal(r.q_sizes, g["q_sizes"].long())
     assert (r.k_iters, r.q_iters) == (g["k_iters"], g["q_iters"])
     assert torch.equal(r.mask, g["mask"])
+
+
+def route_fixture_inputs():
+    """The two steps' inputs of tests/golden/make_route_golden.py (regenerated)."""
+    import sys
+
+    sys.path.insert(0, GOLDEN)
+    try:
+        from make_route_golden import CONFIG, inputs
+    finally:
+        sys.path.remove(GOLDEN)
+    return CONFIG, inputs()
+
+
+def test_two_call_route_matches_reference():
+    """Cold then warm route (D = 128): the oracle core against the reference's own
+    N8V6Core run twice on the CPU: labels, sizes, map and iteration counts exact,
+    centroids to fp32 rounding."""
+    fx = torch.load(os.path.join(GOLDEN, "route_d128_two_calls.pt"))
+    config, steps = route_fixture_inputs()
+    cfg = types.SimpleNamespace(role_q_rank=64, role_k_rank=48, metric_sample_tokens=2048, svg_ear_top_p=0.85,
+                                adaptive_budget_min_density=0.0, adaptive_budget_max_density=1.0, **config)
+    core = oracle.OracleCore(cfg, init_seed=fx["config"]["seed_k"], tol=fx["config"]["tol"])
+    for call, (q, k, v) in zip(fx["calls"], steps):
+        assert [float(t.double().sum()) for t in (q, k, v)] == call["input_sums"]
+        r = core.route(q, k, v)
+        assert torch.equal(r.k_labels, call["k_labels"].long())
+        assert torch.equal(r.q_labels, call["q_labels"].long())
+        assert torch.equal(r.k_sizes, call["k_sizes"].long())
+        assert torch.equal(r.q_sizes, call["q_sizes"].long())
+        assert torch.equal(r.mask, call["mask"])
+        assert (r.k_iters, r.q_iters) == (call["k_iters"], call["q_iters"])
+        for name in ("k_centroids", "v_centroids", "q_centroids"):
+            torch.testing.assert_close(getattr(r, name), call[name].float(), atol=1e-5, rtol=1e-5)

@@ -85,7 +85,7 @@ def test_dense_first_steps_run_dense_and_leave_cache():
 
     dev = torch.device("cuda:0")
     cfg = N8V6Config(num_q_centroids=16, num_k_centroids=24, target_density=0.3, kmeans_iter_init=4,
-                     probe_rows=16, repair_rank=8, role_kv_matmul_precision="highest", kmeans_precision="fp32")
+                     probe_rows=16, repair_rank=16, role_kv_matmul_precision="highest", kmeans_precision="fp32")
     core = N8V6Core(cfg)
     cache = RouteCache(RouteReuseConfig(dense_first_steps=2, route_refresh_every=4))
     q, k, v = synthetic_qkv(2, 128, (4, 8, 8), dtype=torch.bfloat16)
