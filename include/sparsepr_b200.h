@@ -215,6 +215,29 @@ int spr_select_budget(const float* scores, const int32_t* k_sizes, const int32_t
 /* ---------------------------------------------------------------- attention */
 
 /*
+ * Reduced-rank residual repair state of one call (all device pointers, fp32
+ * unless noted; per problem b): x_mean, x_scale, y_mean [bh][d]; left, basis
+ * [bh][d][rank] (rank == 16); alpha the repair strength; probe_rows [bh][m]
+ * the probe token ids in ascending order and probe_dense [bh][m][d] bf16 their
+ * exact rows (m <= 128).  Mirrors the state N8V6Core.repair fits
+ * (src/sparsepr/models/cosmos3/residual_repair.py:263-465) and the arguments
+ * of the fused apply + overwrite kernel it launches
+ * (src/sparsepr/kernels/triton/residual_repair.py:565-653).
+ */
+typedef struct SprRepairState {
+  const float* x_mean;
+  const float* x_scale;
+  const float* y_mean;
+  const float* left;
+  const float* basis;
+  int rank;
+  float alpha;
+  const int32_t* probe_rows;
+  const void* probe_dense;
+  int m;
+} SprRepairState;
+
+/*
  * Block-sparse attention over kept cluster pairs, bf16 in, fp32 accumulate:
  * for query row s of q-cluster c (rows q_offsets[b,c]..q_offsets[b,c+1] of
  * q_perm), softmax(q.K^T/sqrt(d)) V over the key rows of the clusters
@@ -222,18 +245,44 @@ int spr_select_budget(const float* scores, const int32_t* k_sizes, const int32_t
  * k_perm/v_perm).  Rows with no keys output 0.  q_perm [bh,nq,d],
  * k_perm/v_perm [bh,nk,d] bf16, d == 128.  When q_order != NULL the row is
  * stored at out[b, q_order[b,s]] (fused inverse permute), else at out[b,s].
+ * repair (nullable): the repair is applied in the epilogue, each row v (the
+ * bf16-rounded attention row) stored as bf16(v + alpha*((((v - x_mean)/x_scale)
+ * left) basis^T + y_mean)), and the rows of the probe tokens are stored as
+ * their dense rows instead (needs ck <= 1024; tokens are the stored row
+ * indices, i.e. q_order[b,s] when q_order is given).
  * Replaces src/sparsepr/kmeans_utils.py:2164-2350 dynamic_block_sparse_fwd_flashinfer
- * (+ its plan() index build) and kernels/triton/permute.py:235-274.
+ * (+ its plan() index build), kernels/triton/permute.py:235-274 and, with a
+ * repair state, kernels/triton/residual_repair.py:158-254 / 565-653 (fused
+ * apply + probe overwrite).
  */
 int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_perm,
                           const int32_t* q_offsets, const int32_t* k_offsets,
                           const int32_t* sel_ids, const int32_t* sel_counts,
                           int64_t bh, int64_t nq, int64_t nk, int d, int cq, int ck,
-                          const int32_t* q_order, void* out, void* workspace,
-                          size_t workspace_bytes, void* stream);
-
-/* Scratch bytes needed by spr_block_sparse_attn. */
+                          const int32_t* q_order, const SprRepairState* repair, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream);
 size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq);
+
+/*
+ * Probe pre-pass of the fused repair: for the m probe rows of each problem
+ * (rows [bh][m] token ids into the original-order q [bh][n][d] bf16, and
+ * row_cluster [bh][m] their query clusters), attention against every key of
+ * the cluster-sorted k_perm/v_perm [bh][nk][d] in one pass: out_dense [bh][m][d]
+ * the exact dense rows (src/sparsepr/models/common/n8_v6.py:1234-1243) and
+ * out_base [bh][m][d] the rows restricted to the key clusters their query
+ * cluster keeps in routed [bh][cq+1][ck+1] (header row/column first), i.e.
+ * the sparse attention output at those rows, which the repair fit regresses
+ * from (n8_v6.py:1244-1262).  m <= 128, d == 128; the keys are split over
+ * several CTAs per problem and merged in a fixed order; workspace of
+ * spr_probe_rows_attn_workspace_bytes(bh, nk, m) bytes (its first int32 is the
+ * status).
+ */
+size_t spr_probe_rows_attn_workspace_bytes(int64_t bh, int64_t nk, int m);
+int spr_probe_rows_attn(const void* q, const void* k_perm, const void* v_perm, const int32_t* k_offsets,
+                        const uint8_t* routed, const int32_t* rows, const int32_t* row_cluster,
+                        int64_t bh, int64_t n, int64_t nk, int d, int cq, int ck, int m,
+                        void* out_dense, void* out_base, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /*
  * spr_block_sparse_attn without a workspace, for callers that cannot allocate

@@ -52,7 +52,10 @@ PROTOTYPES = {
     "spr_wan_qkv_norm_rope_layout": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _I, C.c_float, _P, _P,
                                           _P, _P]),
     "spr_select_budget": (_I, [_P, _P, _P, _I64, _I, _I, _P, _P, _P, _P]),
-    "spr_block_sparse_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
+    "spr_block_sparse_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P, _P, _SZ,
+                                   _P]),
+    "spr_probe_rows_attn_workspace_bytes": (_SZ, [_I64, _I64, _I]),
+    "spr_probe_rows_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "spr_block_sparse_attn_workspace_bytes": (_SZ, [_I64, _I64, _I]),
     "spr_block_sparse_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]),
     "spr_block_sparse_attn_noalloc_status": (_I, [_P]),
@@ -61,6 +64,13 @@ PROTOTYPES = {
     "spr_chol_solve": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "spr_repair_apply": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _I, _P, _P]),
 }
+
+class SprRepairState(C.Structure):
+    """``SprRepairState`` of include/sparsepr_b200.h (device pointers)."""
+
+    _fields_ = [("x_mean", _P), ("x_scale", _P), ("y_mean", _P), ("left", _P), ("basis", _P), ("rank", _I),
+                ("alpha", _F), ("probe_rows", _P), ("probe_dense", _P), ("m", _I)]
+
 
 _lock = threading.Lock()
 _lib = None

@@ -20,14 +20,25 @@ __all__ = ["sparse_attention", "hunyuan_sparse_attention", "hunyuan_attend", "in
 
 
 def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, attn_events=None,
-                     **route_kw):
+                     return_base: bool = False, fused_repair: bool = False, **route_kw):
     """One SparsePR attention call on [B,H,N,D] Q/K/V.
 
     Returns ``(repaired [B,H,N,D] bf16, density float, info dict)`` like the
-    reference's ``(repaired, density, timings)``.  ``info`` also holds the
-    ``route``, the pre-repair ``base`` output and the ``repair_state``.
-    ``attn_events`` (optional pair of ``torch.cuda.Event``) brackets the
-    block-sparse attention launch on the current stream.
+    reference's ``(repaired, density, timings)``.  With top-p budgets the
+    density is a device scalar read once at the end (a 0-dim tensor while a
+    CUDA graph is being captured).  ``info`` also holds the ``route`` and the
+    ``repair_state``; ``attn_events`` (optional pair of ``torch.cuda.Event``)
+    brackets the block-sparse attention launch on the current stream.
+
+    With ``fused_repair=True`` the repair runs fused into the attention
+    epilogue where the configuration allows it
+    (``N8V6Core.fused_repair_supported``): a probe pre-pass computes the probe
+    rows' exact and sparse outputs in one kernel, the state is fitted from
+    them, and the attention kernel applies it and overwrites the probe rows
+    before its store.  Otherwise the attention output is stored and
+    ``N8V6Core.repair`` applies the repair.
+    ``return_base`` also returns the unrepaired output as ``info["base"]``
+    (an extra attention launch on the fused path; for tests).
     """
     if q.ndim != 4:
         raise RuntimeError(f"sparse_attention expects [B,H,N,D] tensors, got {tuple(q.shape)}.")
@@ -39,15 +50,38 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     route = core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
                        **route_kw)
     bh = batch * heads
-    if attn_events is not None:
-        attn_events[0].record()
-    base = K.block_sparse_attention(
-        route.q_permuted, route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim),
-        route.q_offsets, route.k_offsets, route.selected_ids, route.selected_counts,
-        q_order=route.q_sorted_indices)
-    if attn_events is not None:
-        attn_events[1].record()
-    repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
+    k_perm, v_perm = route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim)
+    base = None
+    if fused_repair and core.fused_repair_supported(route, dim):
+        rows, weights = core.probe_rows(route)
+        q3 = q.to(torch.bfloat16).contiguous().view(bh, tokens, dim)
+        row_cluster = torch.gather(route.q_labels, 1, rows.long())
+        dense, base_probe = K.probe_rows_attention(q3, k_perm, v_perm, route.k_offsets, route.extras["routed"], rows,
+                                                   row_cluster)
+        state, info = core.fit_repair(base_probe, dense, weights, tokens, route)
+        if attn_events is not None:
+            attn_events[0].record()
+        repaired = K.block_sparse_attention(
+            route.q_permuted, k_perm, v_perm, route.q_offsets, route.k_offsets, route.selected_ids,
+            route.selected_counts, q_order=route.q_sorted_indices,
+            repair=(state, core.config.repair_alpha, rows, dense))
+        if attn_events is not None:
+            attn_events[1].record()
+        if return_base:
+            base = K.block_sparse_attention(route.q_permuted, k_perm, v_perm, route.q_offsets, route.k_offsets,
+                                            route.selected_ids, route.selected_counts, q_order=route.q_sorted_indices)
+        repaired = repaired.view(batch, heads, tokens, dim)
+        info["repair_fused"] = True
+        info["probe_base"], info["probe_dense"] = base_probe, dense
+    else:
+        if attn_events is not None:
+            attn_events[0].record()
+        base = K.block_sparse_attention(route.q_permuted, k_perm, v_perm, route.q_offsets, route.k_offsets,
+                                        route.selected_ids, route.selected_counts, q_order=route.q_sorted_indices)
+        if attn_events is not None:
+            attn_events[1].record()
+        repaired, info = core.repair(base.view(batch, heads, tokens, dim), q, k, v, route)
+        info["repair_fused"] = False
     K.collect_status(q.device)
     info["route"] = route
     info["base"] = base
@@ -216,7 +250,7 @@ def sparse_n8_attention_bhld(attn, q_bhld, k_bhld, v_bhld, seq_lens=None):
     del seq_lens
     core = _core_for_cfg_branch(attn)
     out, density, info = sparse_attention(q_bhld, k_bhld, v_bhld, core)
-    for key in ("route", "base", "repair_state"):
+    for key in ("route", "base", "repair_state", "probe_base", "probe_dense"):
         info.pop(key, None)
     dtype = v_bhld.dtype if v_bhld.dtype in (torch.float16, torch.bfloat16) else torch.bfloat16
     return out.to(dtype), density, info

@@ -51,6 +51,54 @@ constexpr int kPairRows = 2 * kTileM;   // query rows per CTA
 constexpr int kSoftmaxThreads = 128;    // per query tile
 constexpr int kThreadsTc = 384;
 constexpr int kMaxRuns = 2048;  // key clusters per problem (ck) this kernel accepts
+constexpr int kMaxRunsRepair = 1024;  // with the fused repair epilogue (its weights take the shared memory)
+constexpr int kRepairRank = 16;
+constexpr int kMaxProbes = 128;
+
+// Kernel modes.
+//   kModePlain : attention output (optionally stored through q_order).
+//   kModeRepair: the same, then the reduced-rank residual repair applied in
+//                the epilogue and probe rows overwritten by their dense rows
+//                (kernels/triton/residual_repair.py:158-254 fused apply +
+//                overwrite, CPU twin models/common/n8_v6.py:1384-1395).
+//   kModeProbe : the probe pre-pass.  Tiles A and B hold the same probe rows
+//                (gathered from the original-order Q); both see every key,
+//                A unmasked (the exact dense rows, n8_v6.py:1234-1243) and B
+//                masked to its row's selected key clusters (the rows' sparse
+//                output, which the repair fit regresses from).
+enum : int { kModePlain = 0, kModeRepair = 1, kModeProbe = 2 };
+
+// Fused repair state (kModeRepair), per problem b:
+//   lfold [b][128][16] = L / x_scale, c0 [b][16] = -sum_d x_mean[d] lfold[d][:],
+//   basis [b][128][16], y_mean [b][128]; probe_tok [b][m] ascending token ids
+//   and probe_dense [b][m][128] their exact rows.
+// out = bf16(v + alpha * (y_mean + (v lfold + c0) basis^T)), v = bf16(attention row).
+struct AttnRepair {
+  const float* lfold;
+  const float* c0;
+  const float* basis;
+  const float* y_mean;
+  const int32_t* probe_tok;
+  const __nv_bfloat16* probe_dense;
+  int m;
+  float alpha;
+};
+
+// Probe pre-pass (kModeProbe), per problem b: rows [b][m] token ids into the
+// original-order Q, row_cluster [b][m] their query clusters, routed [b][cq+1][ck+1]
+// the cluster-pair map (header row/column first).  The keys are split into
+// `splits` contiguous ranges (blockIdx.x); each CTA writes its unnormalised
+// partial rows o_part [b][split][tile][m][128] and (running max, sum) ml_part
+// [b][split][tile][m][2]; probe_merge_kernel combines them.
+struct AttnProbe {
+  const int32_t* rows;
+  const int32_t* row_cluster;
+  const uint8_t* routed;
+  float* o_part;
+  float* ml_part;
+  int m;
+  int splits;
+};
 constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
 constexpr int kSmemTc = 1024 /*align slack*/ + 2 * kTileBytes /*Q_A, Q_B*/ + 4 * kTileBytes /*K,V x2*/;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
@@ -120,36 +168,49 @@ __global__ void tile_table_kernel(const int32_t* __restrict__ q_offsets, int cq,
   tile_start[b * (cq + 1) + cq] = acc;
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(kThreadsTc, 1)
 block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                             const __nv_bfloat16* __restrict__ v, const int32_t* __restrict__ q_offsets,
                             const int32_t* __restrict__ k_offsets, const int32_t* __restrict__ sel_ids,
                             const int32_t* __restrict__ sel_counts, const int32_t* __restrict__ tile_start,
                             int64_t nq, int64_t nk, int cq, int ck, const int32_t* __restrict__ q_order,
-                            __nv_bfloat16* __restrict__ out, float scale_log2, int* __restrict__ err) {
+                            __nv_bfloat16* __restrict__ out, float scale_log2, int* __restrict__ err,
+                            const AttnRepair rep, const AttnProbe prb) {
+  constexpr int kRuns = MODE == kModeRepair ? kMaxRunsRepair : (MODE == kModeProbe ? 1 : kMaxRuns);
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_k_full[2], bar_k_empty[2], bar_v_full[2], bar_v_empty[2], bar_s_full[2], bar_p_full[2],
       bar_o_done[2];
   __shared__ uint32_t s_tmem;
-  __shared__ int32_t s_run_start[kMaxRuns];
-  __shared__ int32_t s_run_end[kMaxRuns + 1];  // inclusive prefix of run lengths
+  __shared__ int32_t s_run_start[kRuns];
+  __shared__ int32_t s_run_end[kRuns + 1];  // inclusive prefix of run lengths
   __shared__ int s_total;
+  // Fused repair weights (kModeRepair only; one element otherwise).
+  constexpr int kRW = MODE == kModeRepair ? kD * kRepairRank : 1;
+  __shared__ __align__(16) float s_lf[kRW], s_bs[kRW];
+  __shared__ float s_c0[MODE == kModeRepair ? kRepairRank : 1], s_ym[MODE == kModeRepair ? kD : 1];
+  __shared__ int32_t s_ptok[MODE == kModeRepair ? kMaxProbes : 1];
 
   const int64_t b = blockIdx.y;
-  const int unit = blockIdx.x;
-  const int32_t* ts = tile_start + b * (cq + 1);
-  if (unit >= ts[cq]) return;  // block-uniform, before any barrier or TMEM use
-  int lo = 0, hi = cq - 1;     // query cluster owning the unit: last c with ts[c] <= unit
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (ts[mid] <= unit) lo = mid; else hi = mid - 1;
+  int c = 0, row0 = 0, rows_a, rows_b;
+  if constexpr (MODE == kModeProbe) {
+    rows_a = rows_b = prb.m;  // one unit per problem: the probe rows in both tiles
+  } else {
+    const int unit = blockIdx.x;
+    const int32_t* ts = tile_start + b * (cq + 1);
+    if (unit >= ts[cq]) return;  // block-uniform, before any barrier or TMEM use
+    int lo = 0, hi = cq - 1;     // query cluster owning the unit: last c with ts[c] <= unit
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (ts[mid] <= unit) lo = mid; else hi = mid - 1;
+    }
+    c = lo;
+    const int32_t qbeg = q_offsets[b * (cq + 1) + c];
+    const int32_t qend = q_offsets[b * (cq + 1) + c + 1];
+    row0 = qbeg + (unit - ts[c]) * kPairRows;
+    rows_a = min(kTileM, qend - row0);
+    rows_b = max(0, min(kTileM, qend - row0 - kTileM));
   }
-  const int c = lo;
-  const int32_t qbeg = q_offsets[b * (cq + 1) + c];
-  const int32_t qend = q_offsets[b * (cq + 1) + c + 1];
-  const int32_t row0 = qbeg + (unit - ts[c]) * kPairRows;
-  const int rows_a = min(kTileM, qend - row0);
-  const int rows_b = max(0, min(kTileM, qend - row0 - kTileM));
   const bool has_b = rows_b > 0;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,8 +222,8 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   const __nv_bfloat16* qb = q + b * nq * kD;
   const __nv_bfloat16* kb = k + b * nk * kD;
   const __nv_bfloat16* vb = v + b * nk * kD;
-  const int32_t* ids = sel_ids + (b * cq + c) * (int64_t)ck;
-  const int nsel = sel_counts[b * cq + c];
+  const int32_t* ids = MODE == kModeProbe ? nullptr : sel_ids + (b * cq + c) * (int64_t)ck;
+  const int nsel = MODE == kModeProbe ? 0 : sel_counts[b * cq + c];
   const int32_t* ko = k_offsets + b * (ck + 1);
 
   if (tid == 0) {
@@ -178,7 +239,25 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     mbar_fence_init();
   }
   if (warp == 8) tmem_alloc<512>(&s_tmem);
-  if (warp == 9) {  // run table of the selected key clusters: start row and prefix length
+  if constexpr (MODE == kModeRepair) {  // repair weights and probe tokens of this problem
+    const int64_t wo = b * (int64_t)(kD * kRepairRank);
+    for (int i = tid; i < kD * kRepairRank; i += kThreadsTc) {
+      s_lf[i] = rep.lfold[wo + i];
+      s_bs[i] = rep.basis[wo + i];
+    }
+    if (tid < kRepairRank) s_c0[tid] = rep.c0[b * kRepairRank + tid];
+    if (tid < kD) s_ym[tid] = rep.y_mean[b * kD + tid];
+    if (tid < rep.m) s_ptok[tid] = rep.probe_tok[b * rep.m + tid];
+  }
+  if (MODE == kModeProbe && warp == 9 && lane == 0) {  // this split's key range: one run over the sorted K/V
+    const int64_t tiles = (nk + kTileN - 1) / kTileN;
+    const int64_t per = (tiles + prb.splits - 1) / prb.splits;
+    const int64_t k0 = min((int64_t)blockIdx.x * per * kTileN, nk), k1 = min(k0 + per * kTileN, nk);
+    s_run_start[0] = (int32_t)k0;
+    s_run_end[0] = (int32_t)(k1 - k0);
+    s_total = (int)(k1 - k0);
+  }
+  if (MODE != kModeProbe && warp == 9) {  // run table of the selected key clusters: start row and prefix length
     int carry = 0;
     for (int base = 0; base < nsel; base += 32) {
       const int i = base + lane;
@@ -202,12 +281,17 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     }
     if (lane == 0) s_total = carry;
   }
-  // Q tiles (all threads), zero rows past the cluster end.
+  // Q tiles (all threads), zero rows past the cluster end.  Probe mode: both
+  // tiles hold the probe rows, gathered from the original-order Q.
   for (int i = tid; i < 2 * kTileM * 16; i += kThreadsTc) {
     const int t = i >> 11, r = (i >> 4) & 127, ch = i & 15;
     const bool ok = r < (t ? rows_b : rows_a);
-    cp_async16(smem_addr(sQ + t * kTileBytes) + sw128_off(r, ch, kTileM),
-               qb + (int64_t)(row0 + t * kTileM + (ok ? r : 0)) * kD + ch * 8, ok);
+    int64_t src_row;
+    if constexpr (MODE == kModeProbe)
+      src_row = ok ? (int64_t)prb.rows[b * prb.m + r] : 0;
+    else
+      src_row = row0 + t * kTileM + (ok ? r : 0);
+    cp_async16(smem_addr(sQ + t * kTileBytes) + sw128_off(r, ch, kTileM), qb + src_row * kD + ch * 8, ok);
   }
   cp_async_commit();
   cp_async_wait_all();
@@ -326,15 +410,26 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     const uint32_t tS = tmem + lane_base + 256 * x, tO = tS + 128;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // Probe mode, tile B: this row's cluster-pair map row and a forward cursor
+    // over the key clusters of the sorted keys.
+    const bool masked = MODE == kModeProbe && x == 1;
+    const uint8_t* maprow = nullptr;
+    int kc_cur = 0;
+    const int key0 = MODE == kModeProbe ? s_run_start[0] : 0;  // first sorted key of this split
+    if (MODE == kModeProbe && masked && row < rows) {
+      const int crow = prb.row_cluster[b * prb.m + row];
+      maprow = prb.routed + ((b * (cq + 1)) + crow + 1) * (int64_t)(ck + 1) + 1;
+    }
     for (int j = 0; j < ntiles && ok; ++j) {
+      const uint32_t tSj = tS;
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_s_full[x], j & 1, err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
       float s[kTileN];
-      tmem_ld32_async(tS, s);  // four loads in flight, one wait
-      tmem_ld32_async(tS + 32, s + 32);
-      tmem_ld32_async(tS + 64, s + 64);
-      tmem_ld32_async(tS + 96, s + 96);
+      tmem_ld32_async(tSj, s);  // four loads in flight, one wait
+      tmem_ld32_async(tSj + 32, s + 32);
+      tmem_ld32_async(tSj + 64, s + 64);
+      tmem_ld32_async(tSj + 96, s + 96);
       tmem_wait_ld();
       reg_fence32(s);
       reg_fence32(s + 32);
@@ -344,6 +439,35 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       if (valid < kTileN) {  // only the last tile of a cluster is partial (warp-uniform)
 #pragma unroll
         for (int i = 0; i < kTileN; ++i) s[i] = i < valid ? s[i] : -INFINITY;
+      }
+      if (MODE == kModeProbe && masked) {
+        // Keys of this tile that lie in a key cluster this row's query
+        // cluster keeps; the cluster segments are the same for every row.
+        uint32_t keep[4] = {0u, 0u, 0u, 0u};
+        const int t0 = key0 + j * kTileN, t1 = min(t0 + kTileN, key0 + total);
+        if (j == 0) {  // first tile of this split: the key cluster holding t0 by binary search
+          int lo2 = 0, hi2 = ck - 1;  // last kc with ko[kc] <= t0
+          while (lo2 < hi2) {
+            const int mid = (lo2 + hi2 + 1) >> 1;
+            if (ko[mid] <= t0) lo2 = mid; else hi2 = mid - 1;
+          }
+          kc_cur = lo2;
+        }
+        while (ko[kc_cur + 1] <= t0) ++kc_cur;
+        for (int pos = t0, kc = kc_cur; pos < t1; ++kc) {
+          const int seg_end = min((int)ko[kc + 1], t1);
+          if (seg_end > pos && maprow && maprow[kc]) {
+            const int lo_i = pos - t0, hi_i = seg_end - t0;  // bits [lo_i, hi_i) of the tile
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const int a0 = max(lo_i - 32 * w, 0), a1 = min(hi_i - 32 * w, 32);
+              if (a1 > a0) keep[w] |= (a1 - a0 == 32 ? 0xffffffffu : ((1u << (a1 - a0)) - 1u)) << a0;
+            }
+          }
+          pos = max(pos, seg_end);
+        }
+#pragma unroll
+        for (int i = 0; i < kTileN; ++i) s[i] = ((keep[i >> 5] >> (i & 31)) & 1u) ? s[i] : -INFINITY;
       }
       float m8[8];  // eight independent max chains, two scores per instruction
 #pragma unroll
@@ -360,7 +484,10 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
         alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - mx);
         m_run = mx;
       }
-      const unsigned long long sc2 = pk2(scale_log2, scale_log2), nm2 = pk2(-m_run, -m_run);
+      // A row whose keys so far are all masked (probe mode) keeps m = -inf and
+      // exponentiates against 0 instead: every p is 0 and no NaN appears.
+      const float m_use = MODE == kModeProbe && m_run == -INFINITY ? 0.f : m_run;
+      const unsigned long long sc2 = pk2(scale_log2, scale_log2), nm2 = pk2(-m_use, -m_use);
       unsigned long long sum2[4] = {0ull, 0ull, 0ull, 0ull};  // packed partial sums (+0.0f pairs)
       // P(j) over the first 64 columns of S(j) (already loaded above), in two
       // 64-key halves stored as soon as each is packed.
@@ -381,7 +508,7 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           __nv_bfloat162 hh = __floats2bfloat162_rn(p0, p1);
           pk[(i - 64 * hf) >> 1] = *reinterpret_cast<uint32_t*>(&hh);
         }
-        tmem_st32(tS + 32 * hf, reinterpret_cast<const float*>(pk));
+        tmem_st32(tSj + 32 * hf, reinterpret_cast<const float*>(pk));
       }
       float a0, a1, b0, b1;
       up2(add2(sum2[0], sum2[1]), a0, a1);
@@ -408,28 +535,155 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     const bool have = __all_sync(0xffffffffu, ok && ntiles > 0);
     tc_fence_after();
     const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
-    const int64_t s_row = row0 + x * kTileM + row;
-    const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
-    uint4* orow = reinterpret_cast<uint4*>(out + (b * nq + dst) * kD);
+    if constexpr (MODE == kModeProbe) {
+      // Unnormalised partial rows of this key split (tile A: all keys, tile B:
+      // the kept ones).  A row that saw no kept key reports l = 0.
+      const bool any = have && m_run != -INFINITY;
+      const int64_t pr = ((b * prb.splits + blockIdx.x) * 2 + x) * (int64_t)prb.m + (row < rows ? row : 0);
+      float4* orow = reinterpret_cast<float4*>(prb.o_part + pr * kD);
 #pragma unroll
-    for (int cb = 0; cb < 4; ++cb) {
-      float o[32];
-      if (have) {
-        tmem_ld32(tO + cb * 32, o);
-      } else {
+      for (int cb = 0; cb < 4; ++cb) {
+        float o[32];
+        if (have) {
+          tmem_ld32(tO + cb * 32, o);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (row < rows) {
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            orow[cb * 8 + q4] = any ? make_float4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3])
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
       if (row < rows) {
+        prb.ml_part[2 * pr] = any ? m_run : -INFINITY;
+        prb.ml_part[2 * pr + 1] = any ? l_run : 0.f;
+      }
+    } else if constexpr (MODE == kModeRepair) {
+      // v = bf16(O / l); coords = v L' + c0 (first pass over O); then
+      // out = bf16(v + alpha (y_mean + coords B^T)) (second pass), or the
+      // exact dense row for a probe token.  Same operation order as the
+      // standalone repair apply, so the result equals attention-then-apply.
+      const int64_t s_row = row0 + x * kTileM + row;
+      const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
+      // coords as packed pairs (j, j+1); each lane of an f32x2 FMA rounds like fmaf.
+      unsigned long long cp2[kRepairRank / 2];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t w[4];
+      for (int jr = 0; jr < kRepairRank / 2; ++jr) cp2[jr] = pk2(s_c0[2 * jr], s_c0[2 * jr + 1]);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 hh = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
-            w[e] = *reinterpret_cast<uint32_t*>(&hh);
+      for (int cb = 0; cb < 4; ++cb) {
+        float o[32];
+        if (have) {
+          tmem_ld32(tO + cb * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float vv = __bfloat162float(__float2bfloat16_rn(o[i] * inv));
+          const unsigned long long vv2 = pk2(vv, vv);
+          const float4* lf = reinterpret_cast<const float4*>(s_lf + (cb * 32 + i) * kRepairRank);
+#pragma unroll
+          for (int q4 = 0; q4 < kRepairRank / 4; ++q4) {
+            const float4 l4 = lf[q4];
+            cp2[2 * q4] = fma2(vv2, pk2(l4.x, l4.y), cp2[2 * q4]);
+            cp2[2 * q4 + 1] = fma2(vv2, pk2(l4.z, l4.w), cp2[2 * q4 + 1]);
           }
-          orow[cb * 4 + q4] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      unsigned long long cc2[kRepairRank];  // (coord_j, coord_j) for the second pass
+#pragma unroll
+      for (int jr = 0; jr < kRepairRank / 2; ++jr) {
+        float c_lo, c_hi;
+        up2(cp2[jr], c_lo, c_hi);
+        cc2[2 * jr] = pk2(c_lo, c_lo);
+        cc2[2 * jr + 1] = pk2(c_hi, c_hi);
+      }
+      // Probe token?  (s_ptok ascending; -1 when not found.)
+      int probe = -1;
+      {
+        int plo = 0, phi = rep.m - 1;
+        while (plo <= phi) {
+          const int mid = (plo + phi) >> 1;
+          const int32_t tv = s_ptok[mid];
+          if (tv == (int32_t)dst) { probe = mid; break; }
+          if (tv < (int32_t)dst) plo = mid + 1; else phi = mid - 1;
+        }
+      }
+      uint4* orow = reinterpret_cast<uint4*>(out + (b * nq + dst) * kD);
+      const uint4* prow = reinterpret_cast<const uint4*>(rep.probe_dense + (b * rep.m + max(probe, 0)) * (int64_t)kD);
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float o[32];
+        if (have) {
+          tmem_ld32(tO + cb * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (row < rows) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 w4;
+            if (probe >= 0) {
+              w4 = prow[cb * 4 + q4];
+            } else {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                // Output columns d, d+1 as one packed pair: y_mean + sum_j coord_j B[.][j] in j order.
+                const int dcol = cb * 32 + q4 * 8 + 2 * e;
+                const float4* bs0 = reinterpret_cast<const float4*>(s_bs + dcol * kRepairRank);
+                const float4* bs1 = reinterpret_cast<const float4*>(s_bs + (dcol + 1) * kRepairRank);
+                unsigned long long acc2 = pk2(s_ym[dcol], s_ym[dcol + 1]);
+#pragma unroll
+                for (int q = 0; q < kRepairRank / 4; ++q) {
+                  const float4 b0 = bs0[q], b1 = bs1[q];
+                  acc2 = fma2(cc2[4 * q], pk2(b0.x, b1.x), acc2);
+                  acc2 = fma2(cc2[4 * q + 1], pk2(b0.y, b1.y), acc2);
+                  acc2 = fma2(cc2[4 * q + 2], pk2(b0.z, b1.z), acc2);
+                  acc2 = fma2(cc2[4 * q + 3], pk2(b0.w, b1.w), acc2);
+                }
+                const float v0 = __bfloat162float(__float2bfloat16_rn(o[q4 * 8 + 2 * e] * inv));
+                const float v1 = __bfloat162float(__float2bfloat16_rn(o[q4 * 8 + 2 * e + 1] * inv));
+                float a0, a1;
+                up2(fma2(pk2(rep.alpha, rep.alpha), acc2, pk2(v0, v1)), a0, a1);
+                __nv_bfloat162 hh = __floats2bfloat162_rn(a0, a1);
+                w[e] = *reinterpret_cast<uint32_t*>(&hh);
+              }
+              w4 = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            orow[cb * 4 + q4] = w4;
+          }
+        }
+      }
+    } else {
+      const int64_t s_row = row0 + x * kTileM + row;
+      const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
+      uint4* orow = reinterpret_cast<uint4*>(out + (b * nq + dst) * kD);
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float o[32];
+        if (have) {
+          tmem_ld32(tO + cb * 32, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (row < rows) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 hh = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
+              w[e] = *reinterpret_cast<uint32_t*>(&hh);
+            }
+            orow[cb * 4 + q4] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
         }
       }
     }
@@ -445,45 +699,181 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 }  // namespace spr
 
 namespace spr {
-static int set_attn_smem_attr();
+
+// Fold the standardisation into the left factor: lfold[b][d][j] = L[b][d][j] / xs[b][d]
+// (correctly rounded division) and c0[b][j] = -sum_d xm[b][d] lfold[b][d][j] in d order.
+__global__ void repair_fold_kernel(const float* __restrict__ xm, const float* __restrict__ xs,
+                                   const float* __restrict__ left, float* __restrict__ lfold, float* __restrict__ c0) {
+  const int64_t b = blockIdx.x;
+  __shared__ float sh[kD * kRepairRank];
+  for (int i = threadIdx.x; i < kD * kRepairRank; i += blockDim.x) {
+    const float v = __fdiv_rn(left[b * kD * kRepairRank + i], xs[b * kD + i / kRepairRank]);
+    sh[i] = v;
+    lfold[b * kD * kRepairRank + i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kRepairRank) {
+    float c = 0.f;
+    for (int d = 0; d < kD; ++d) c = fmaf(-xm[b * kD + d], sh[d * kRepairRank + threadIdx.x], c);
+    c0[b * kRepairRank + threadIdx.x] = c;
+  }
+}
+
+// Combine the key splits of the probe pre-pass, per (b, tile, row) and column:
+// M = max_s m_s, out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s in split
+// order (0 when no split saw a kept key), rounded to bf16.  Tile 0 -> out_dense,
+// tile 1 -> out_base.
+__global__ void probe_merge_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part, int splits,
+                                   int m, __nv_bfloat16* __restrict__ out_dense, __nv_bfloat16* __restrict__ out_base) {
+  const int r = blockIdx.x, x = blockIdx.y, col = threadIdx.x;
+  const int64_t b = blockIdx.z;
+  float mx = -INFINITY;
+  for (int sp = 0; sp < splits; ++sp) mx = fmaxf(mx, ml_part[2 * (((b * splits + sp) * 2 + x) * (int64_t)m + r)]);
+  float l = 0.f, acc = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const int64_t pr = ((b * splits + sp) * 2 + x) * (int64_t)m + r;
+    const float ms = ml_part[2 * pr];
+    if (ms == -INFINITY) continue;
+    const float w = exp2f(ms - mx);
+    l = fmaf(w, ml_part[2 * pr + 1], l);
+    acc = fmaf(w, o_part[pr * kD + col], acc);
+  }
+  __nv_bfloat16* dst = x ? out_base : out_dense;
+  dst[(b * m + r) * kD + col] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+}
+
+template <int MODE>
+static int launch_attn(dim3 grid, const void* q, const void* k, const void* v, const int32_t* q_offsets,
+                       const int32_t* k_offsets, const int32_t* sel_ids, const int32_t* sel_counts,
+                       const int32_t* tile_start, int64_t nq, int64_t nk, int d, int cq, int ck,
+                       const int32_t* q_order, void* out, int* err, const AttnRepair& rep, const AttnProbe& prb,
+                       cudaStream_t st) {
+  const cudaError_t e =
+      cudaFuncSetAttribute(block_sparse_attn_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
+  if (e != cudaSuccess)
+    return fail(SPR_ERR_LAUNCH, "block-sparse attention: shared-memory opt-in (%d B): %s", kSmemTc,
+                cudaGetErrorString(e));
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
+  block_sparse_attn_tc_kernel<MODE><<<grid, kThreadsTc, kSmemTc, st>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, q_offsets, k_offsets, sel_ids,
+      sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err, rep, prb);
+  return check_launch(MODE == kModeProbe ? "probe rows attention" : "block-sparse attention");
+}
 }  // namespace spr
 
 using namespace spr;
 
+static size_t repair_fold_floats(int64_t bh) { return (size_t)bh * (kD * kRepairRank + kRepairRank); }
+
 extern "C" size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq) {
   (void)nq;
-  return 256 + align_up((size_t)bh * (cq + 1) * sizeof(int32_t), 256) + 256;
+  return 256 + align_up((size_t)bh * (cq + 1) * sizeof(int32_t), 256) + 256 +
+         align_up(repair_fold_floats(bh) * sizeof(float), 256) + 256;
 }
 
 extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, const void* v_perm,
                                      const int32_t* q_offsets, const int32_t* k_offsets, const int32_t* sel_ids,
                                      const int32_t* sel_counts, int64_t bh, int64_t nq, int64_t nk, int d, int cq,
-                                     int ck, const int32_t* q_order, void* out, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
+                                     int ck, const int32_t* q_order, const SprRepairState* repair, void* out,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
   if (d != kD) return fail(SPR_ERR_SHAPE, "block-sparse attention requires d=128, got %d", d);
   if (ck > kMaxRuns) return fail(SPR_ERR_SHAPE, "block-sparse attention: ck=%d exceeds %d", ck, kMaxRuns);
   if (bh <= 0 || nq <= 0 || nk <= 0 || cq <= 0 || ck <= 0 || bh > 65535 || nq > INT32_MAX || nk > INT32_MAX)
     return fail(SPR_ERR_SHAPE, "block-sparse attention: bad shape");
   if (!aligned(q_perm, 16) || !aligned(k_perm, 16) || !aligned(v_perm, 16) || !aligned(out, 16))
     return fail(SPR_ERR_ALIGN, "block-sparse attention: 16-byte alignment required");
+  if (repair) {
+    if (repair->rank != kRepairRank)
+      return fail(SPR_ERR_SHAPE, "fused repair: rank %d unsupported (16)", repair->rank);
+    if (ck > kMaxRunsRepair)
+      return fail(SPR_ERR_SHAPE, "fused repair: ck=%d exceeds %d", ck, kMaxRunsRepair);
+    if (repair->m < 0 || repair->m > kMaxProbes || (repair->m > 0 && (!repair->probe_rows || !repair->probe_dense)))
+      return fail(SPR_ERR_SHAPE, "fused repair: m=%d probe rows (0..%d, rows and dense rows given)", repair->m,
+                  kMaxProbes);
+    if (!repair->x_mean || !repair->x_scale || !repair->y_mean || !repair->left || !repair->basis)
+      return fail(SPR_ERR_ARG, "fused repair: null state tensor");
+    if (repair->m > 0 && !aligned(repair->probe_dense, 16))
+      return fail(SPR_ERR_ALIGN, "fused repair: dense probe rows must be 16-byte aligned");
+  }
   Carver cv(workspace, workspace_bytes);
   int* err = cv.take<int>(64);
   int32_t* tile_start = cv.take<int32_t>((size_t)bh * (cq + 1));
+  float* fold = cv.take<float>(repair_fold_floats(bh));
   if (!workspace || !cv.ok())
     return fail(SPR_ERR_WORKSPACE, "block-sparse attention: workspace %zu < %zu", workspace_bytes, cv.off);
   cudaStream_t st = (cudaStream_t)stream;
   tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   int s = check_launch("attention tile table");
   if (s) return s;
-  if ((s = set_attn_smem_attr())) return s;
   // Upper bound on 256-row units per problem: every cluster may add one partial unit.
   const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
-  dim3 grid((unsigned)max_tiles, (unsigned)bh);
-  const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
-  block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
-      (const __nv_bfloat16*)q_perm, (const __nv_bfloat16*)k_perm, (const __nv_bfloat16*)v_perm, q_offsets, k_offsets,
-      sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
-  return check_launch("block-sparse attention");
+  const dim3 grid((unsigned)max_tiles, (unsigned)bh);
+  AttnProbe prb{};
+  AttnRepair rep{};
+  if (!repair)
+    return launch_attn<kModePlain>(grid, q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
+                                   tile_start, nq, nk, d, cq, ck, q_order, out, err, rep, prb, st);
+  float* lfold = fold;
+  float* c0 = fold + (size_t)bh * kD * kRepairRank;
+  repair_fold_kernel<<<(unsigned)bh, 256, 0, st>>>(repair->x_mean, repair->x_scale, repair->left, lfold, c0);
+  if ((s = check_launch("fused repair: fold"))) return s;
+  rep.lfold = lfold;
+  rep.c0 = c0;
+  rep.basis = repair->basis;
+  rep.y_mean = repair->y_mean;
+  rep.probe_tok = repair->probe_rows;
+  rep.probe_dense = (const __nv_bfloat16*)repair->probe_dense;
+  rep.m = repair->m;
+  rep.alpha = repair->alpha;
+  return launch_attn<kModeRepair>(grid, q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
+                                  tile_start, nq, nk, d, cq, ck, q_order, out, err, rep, prb, st);
+}
+
+// Key splits of the probe pre-pass: about two CTAs per SM over all problems,
+// at most 16 per problem and at least 4 key tiles per split.
+static int probe_splits(int64_t bh, int64_t nk) {
+  const int64_t tiles = (nk + kTileN - 1) / kTileN;
+  int64_t sp = std::max<int64_t>(1, (2 * 148) / bh);
+  sp = std::min<int64_t>(sp, 16);
+  sp = std::min<int64_t>(sp, std::max<int64_t>(1, tiles / 4));
+  return (int)sp;
+}
+
+extern "C" size_t spr_probe_rows_attn_workspace_bytes(int64_t bh, int64_t nk, int m) {
+  const size_t part = (size_t)bh * probe_splits(bh, nk) * 2 * (size_t)m;
+  return 256 + align_up(part * kD * sizeof(float), 256) + align_up(part * 2 * sizeof(float), 256) + 256;
+}
+
+extern "C" int spr_probe_rows_attn(const void* q, const void* k_perm, const void* v_perm, const int32_t* k_offsets,
+                                   const uint8_t* routed, const int32_t* rows, const int32_t* row_cluster,
+                                   int64_t bh, int64_t n, int64_t nk, int d, int cq, int ck, int m, void* out_dense,
+                                   void* out_base, void* workspace, size_t workspace_bytes, void* stream) {
+  if (d != kD) return fail(SPR_ERR_SHAPE, "probe rows attention requires d=128, got %d", d);
+  if (bh <= 0 || n <= 0 || nk <= 0 || cq <= 0 || ck <= 0 || bh > 65535 || n > INT32_MAX || nk > INT32_MAX)
+    return fail(SPR_ERR_SHAPE, "probe rows attention: bad shape");
+  if (m <= 0 || m > kTileM) return fail(SPR_ERR_SHAPE, "probe rows attention: m=%d must be in [1,%d]", m, kTileM);
+  if (!aligned(q, 16) || !aligned(k_perm, 16) || !aligned(v_perm, 16) || !aligned(out_dense, 16) ||
+      !aligned(out_base, 16))
+    return fail(SPR_ERR_ALIGN, "probe rows attention: 16-byte alignment required");
+  const int splits = probe_splits(bh, nk);
+  const size_t part = (size_t)bh * splits * 2 * (size_t)m;
+  Carver cv(workspace, workspace_bytes);
+  int* err = cv.take<int>(64);
+  float* o_part = cv.take<float>(part * kD);
+  float* ml_part = cv.take<float>(part * 2);
+  if (!workspace || !cv.ok())
+    return fail(SPR_ERR_WORKSPACE, "probe rows attention: workspace %zu < %zu", workspace_bytes, cv.off);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaMemsetAsync(err, 0, sizeof(int), st);
+  AttnProbe prb{rows, row_cluster, routed, o_part, ml_part, m, splits};
+  AttnRepair rep{};
+  int s = launch_attn<kModeProbe>(dim3((unsigned)splits, (unsigned)bh), q, k_perm, v_perm, nullptr, k_offsets,
+                                  nullptr, nullptr, nullptr, n, nk, d, cq, ck, nullptr, nullptr, err, rep, prb, st);
+  if (s) return s;
+  probe_merge_kernel<<<dim3((unsigned)m, 2, (unsigned)bh), kD, 0, st>>>(o_part, ml_part, splits, m,
+                                                                       (__nv_bfloat16*)out_dense,
+                                                                       (__nv_bfloat16*)out_base);
+  return check_launch("probe rows attention: merge");
 }
 
 // ---------------------------------------------------------------------------
@@ -520,14 +910,6 @@ static int noalloc_scratch(int32_t** out) {
   return SPR_OK;
 }
 
-static int set_attn_smem_attr() {
-  const cudaError_t e =
-      cudaFuncSetAttribute(block_sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
-  if (e != cudaSuccess)
-    return fail(SPR_ERR_LAUNCH, "block-sparse attention: shared-memory opt-in (%d B): %s", kSmemTc,
-                cudaGetErrorString(e));
-  return SPR_OK;
-}
 }  // namespace spr
 
 extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_perm, const void* v_perm,
@@ -554,14 +936,12 @@ extern "C" int spr_block_sparse_attn_noalloc(const void* q_perm, const void* k_p
   cudaStream_t st = (cudaStream_t)stream;
   tile_table_kernel<<<(unsigned)bh, 32, 0, st>>>(q_offsets, cq, tile_start, err);
   if ((s = check_launch("attention tile table"))) return s;
-  if ((s = set_attn_smem_attr())) return s;
   const int64_t max_tiles = (nq + kPairRows - 1) / kPairRows + cq;
-  dim3 grid((unsigned)max_tiles, (unsigned)bh);
-  const float scale_log2 = 1.4426950408889634f / sqrtf((float)d);
-  block_sparse_attn_tc_kernel<<<grid, kThreadsTc, kSmemTc, st>>>(
-      (const __nv_bfloat16*)q_perm, (const __nv_bfloat16*)k_perm, (const __nv_bfloat16*)v_perm, q_offsets, k_offsets,
-      sel_ids, sel_counts, tile_start, nq, nk, cq, ck, q_order, (__nv_bfloat16*)out, scale_log2, err);
-  return check_launch("block-sparse attention (no-alloc)");
+  AttnProbe prb{};
+  AttnRepair rep{};
+  return launch_attn<kModePlain>(dim3((unsigned)max_tiles, (unsigned)bh), q_perm, k_perm, v_perm, q_offsets,
+                                 k_offsets, sel_ids, sel_counts, tile_start, nq, nk, d, cq, ck, q_order, out, err,
+                                 rep, prb, st);
 }
 
 extern "C" int spr_block_sparse_attn_noalloc_status(int* out) {

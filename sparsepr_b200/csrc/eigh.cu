@@ -330,7 +330,8 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
   if (n == 64 || n == 128) {
     const int big = n * (n + 1) * (int)sizeof(float);
     auto kern = n == 64 ? sym_eig_big_kernel<64> : sym_eig_big_kernel<128>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+    if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "sym_eig: shared-memory opt-in: %s", cudaGetErrorString(e));
     kern<<<(unsigned)batch, kEigBigThreads, big, st>>>(a, evals, evecs, max_sweeps, tol);
     return check_launch("sym_eig");
   }

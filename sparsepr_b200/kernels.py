@@ -301,8 +301,14 @@ def select_budget(scores: torch.Tensor, k_sizes: torch.Tensor, budgets: torch.Te
 
 def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
                            q_order: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                           _ws_tag: str = "attn") -> torch.Tensor:
-    """Block-sparse attention over kept cluster pairs (bf16, d=128) -> [B,Nq,D] bf16."""
+                           _ws_tag: str = "attn", repair=None) -> torch.Tensor:
+    """Block-sparse attention over kept cluster pairs (bf16, d=128) -> [B,Nq,D] bf16.
+
+    ``repair`` (optional) = ``(state, alpha, probe_rows, probe_dense)`` with
+    ``state = (x_mean, x_scale, y_mean, left, basis)`` (rank 16): the repair is
+    applied in the kernel's epilogue and the probe rows are stored as their
+    dense rows (``probe_rows`` [B,M] token ids in any order, ``probe_dense``
+    [B,M,D] bf16)."""
     dev = _cuda(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts)
     b, nq, d = q_perm.shape
     nk = k_perm.shape[1]
@@ -316,15 +322,60 @@ def block_sparse_attention(q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids
         out = torch.empty_like(q_perm)
     nbytes = _lib.query("spr_block_sparse_attn_workspace_bytes", b, nq, cq)
     ws = workspace(dev, nbytes, _ws_tag)
+    rs = None
+    keep = ()
+    if repair is not None:
+        import ctypes
+
+        state, alpha, rows, dense = repair
+        xm, xs, ym, left, basis = (t.to(torch.float32).contiguous() for t in state)
+        if left.shape[-1] != 16 or left.shape[0] != b:
+            raise RuntimeError(f"fused repair needs rank-16 state for {b} problems, got left {tuple(left.shape)}")
+        # The kernel looks probe tokens up by binary search: ascending order.
+        srt, perm = torch.sort(rows.to(torch.int32), dim=1)
+        dense_s = torch.gather(dense.to(torch.bfloat16), 1, perm.unsqueeze(-1).expand(-1, -1, d)).contiguous()
+        srt = srt.contiguous()
+        keep = (xm, xs, ym, left, basis, srt, dense_s)
+        rs = _lib.SprRepairState(_p(xm), _p(xs), _p(ym), _p(left), _p(basis), 16, float(alpha), _p(srt),
+                                 _p(dense_s), int(srt.shape[1]))
+        _count(1)
     _count(2)
     _lib.call("spr_block_sparse_attn", _p(q_perm), _p(k_perm), _p(v_perm), _p(q_offsets), _p(k_offsets), _p(sel_ids),
-              _p(sel_counts), b, nq, nk, d, cq, ck, _p(q_order), _p(out), _p(ws), ws.numel(), _stream(dev))
+              _p(sel_counts), b, nq, nk, d, cq, ck, _p(q_order), None if rs is None else ctypes.byref(rs), _p(out),
+              _p(ws), ws.numel(), _stream(dev))
+    del keep  # the launch is enqueued; the caching allocator keeps the memory stream-ordered
     return out
+
+
+def probe_rows_attention(q, k_perm, v_perm, k_offsets, routed, rows, row_cluster):
+    """The probe pre-pass of the fused repair: ``(dense [B,M,D], base [B,M,D])`` bf16
+    for probe rows ``rows`` [B,M] of the original-order ``q`` [B,N,D]: exact
+    attention against all keys, and attention restricted to the key clusters
+    that ``routed`` [B,Cq+1,Ck+1] keeps for their query clusters ``row_cluster``."""
+    dev = _cuda(q, k_perm, v_perm, k_offsets, routed, rows, row_cluster)
+    b, n, d = q.shape
+    nk = k_perm.shape[1]
+    m = rows.shape[1]
+    cq, ck = routed.shape[1] - 1, routed.shape[2] - 1
+    for name, t in (("q", q), ("k_perm", k_perm), ("v_perm", v_perm)):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"{name} must be bf16, got {t.dtype}")
+        _contig(name, t)
+    dense = torch.empty((b, m, d), dtype=torch.bfloat16, device=dev)
+    base = torch.empty_like(dense)
+    ws = workspace(dev, _lib.query("spr_probe_rows_attn_workspace_bytes", b, nk, m), "attn_probe")
+    ri = rows.to(torch.int32).contiguous()
+    rc = row_cluster.to(torch.int32).contiguous()
+    mp = routed.contiguous().view(torch.uint8)
+    _count(2)
+    _lib.call("spr_probe_rows_attn", _p(q), _p(k_perm), _p(v_perm), _p(_contig("k_offsets", k_offsets)), _p(mp),
+              _p(ri), _p(rc), b, n, nk, d, cq, ck, m, _p(dense), _p(base), _p(ws), ws.numel(), _stream(dev))
+    return dense, base
 
 
 # Per device: (device int32[5] snapshot, pinned host copy, event of the copy).
 _STATUS: dict[tuple, tuple] = {}
-STATUS_WORDS = ("kmeans", "attention", "dense_rows", "role_projection", "attention_mass_scores")
+STATUS_WORDS = ("kmeans", "attention", "dense_rows", "role_projection", "attention_mass_scores", "probe_rows")
 
 
 def collect_status(dev: torch.device) -> None:
@@ -349,6 +400,9 @@ def collect_status(dev: torch.device) -> None:
     st = _stream(dev)
     _lib.call("spr_role_projection_status_async", buf[3:4].data_ptr(), st)
     _lib.call("spr_attention_mass_scores_status_async", buf[4:5].data_ptr(), st)
+    ws = _WS.get((dev.type, dev.index, _SCOPE[0], "attn_probe"))
+    if ws is not None:
+        buf[5:6].copy_(ws[:4].view(torch.int32))
     host.copy_(buf, non_blocking=True)
     ev.record()
 

@@ -694,6 +694,57 @@ class N8V6Core:
         return route
 
     # -- repair --------------------------------------------------------------
+    def probe_rows(self, route: N8V6Route):
+        """Probe rows and weights of ``route`` (selected once, cached on the route;
+        ``residual_repair.py:118-260``)."""
+        cfg = self.config
+        if route.probe_rows is not None and route.probe_weights is not None:
+            return route.probe_rows, route.probe_weights
+        if cfg.probe_selection_policy == "first_token_largest_groups":
+            rows, weights = select_first_token_largest_groups(route.q_role_features, route.q_labels,
+                                                              cfg.num_q_centroids, cfg.probe_rows)
+        else:
+            rows, weights = select_role_equal_probes(route.q_role_features, route.q_labels, cfg.num_q_centroids,
+                                                     cfg.probe_rows, order=route.q_sorted_indices,
+                                                     offsets=route.q_offsets)
+        route.probe_rows, route.probe_weights = rows, weights
+        return rows, weights
+
+    def fit_repair(self, base_probe, dense, weights, tokens: int, route: N8V6Route):
+        """Fit the repair state from the probe rows' sparse output ``base_probe``
+        and exact rows ``dense`` ([BH,M,D]); per-head recovery of a non-finite fit
+        (``n8_v6.py:1244-1377``).  Returns ``(state, info)``."""
+        cfg = self.config
+        count, dim = int(base_probe.shape[1]), int(base_probe.shape[2])
+        y_fit = dense.float() - base_probe.float()
+        rank = min(cfg.repair_rank, count, dim)
+        state = fit_reduced_rank_residual(base_probe.float(), y_fit, weights, rank, cfg.repair_ridge)
+        state, self.repair_recovery_mask, policy = recover_nonfinite_rrr_state(state, self.repair_state_current)
+        self.repair_state_current = state
+        info = {
+            "probe_rows": count,
+            "probe_selection_policy": cfg.probe_selection_policy,
+            "repair_rank": rank,
+            "repair_feature_dim": dim,
+            "repair_features": cfg.repair_features,
+            "repair_basis_source": cfg.repair_basis_source,
+            "repair_backend": "sparsepr_b200",
+            "repair_recovery_policy": policy,
+            "effective_video_density": _clamp_density(route.base_video_density + count / float(tokens)),
+        }
+        return state, info
+
+    def fused_repair_supported(self, route: N8V6Route, dim: int) -> bool:
+        """Whether the repair can run inside the attention epilogue
+        (``spr_block_sparse_attn`` with a repair state): rank 16, d = 128,
+        at most 128 probes and 1024 key clusters, output features, no norm cap."""
+        cfg = self.config
+        count = min(max(1, int(cfg.probe_rows)), int(route.q_labels.shape[1]))
+        return (dim == 128 and min(cfg.repair_rank, count, dim) == 16 and count <= 128
+                and route.k_offsets is not None and route.k_offsets.shape[-1] - 1 <= 1024
+                and cfg.repair_norm_cap == 0.0 and cfg.repair_features == "output"
+                and "routed" in route.extras and not route.permuted_includes_suffix)
+
     def repair(self, base_video, q_video, k_full, v_full, route: N8V6Route):
         """Probe-fitted residual repair of video rows (``n8_v6.py:1174-1444``).
 
@@ -706,39 +757,13 @@ class N8V6Core:
         if cfg.repair_norm_cap > 0.0 or cfg.repair_features != "output":
             raise NotImplementedError("sparsepr_b200 repair implements output features without a norm cap.")
         base = base_video.to(torch.bfloat16).contiguous().view(bh, tokens, dim)
-        if route.probe_rows is not None and route.probe_weights is not None:
-            rows, weights = route.probe_rows, route.probe_weights
-        else:
-            if cfg.probe_selection_policy == "first_token_largest_groups":
-                rows, weights = select_first_token_largest_groups(route.q_role_features, route.q_labels,
-                                                                  cfg.num_q_centroids, cfg.probe_rows)
-            else:
-                rows, weights = select_role_equal_probes(route.q_role_features, route.q_labels, cfg.num_q_centroids,
-                                                         cfg.probe_rows, order=route.q_sorted_indices,
-                                                         offsets=route.q_offsets)
-            route.probe_rows, route.probe_weights = rows, weights
-        count = int(rows.shape[1])
+        rows, weights = self.probe_rows(route)
         q = q_video.to(torch.bfloat16).contiguous().view(bh, tokens, dim)
         kf = k_full.to(torch.bfloat16).contiguous().view(bh, -1, dim)
         vf = v_full.to(torch.bfloat16).contiguous().view(bh, -1, dim)
         gidx = rows.unsqueeze(2).expand(-1, -1, dim)
         dense = K.dense_attention_rows(torch.gather(q, 1, gidx), kf, vf)
-        base_probe = torch.gather(base, 1, gidx).float()
-        y_fit = dense.float() - base_probe
-        rank = min(cfg.repair_rank, count, dim)
-        state = fit_reduced_rank_residual(base_probe, y_fit, weights, rank, cfg.repair_ridge)
-        state, self.repair_recovery_mask, policy = recover_nonfinite_rrr_state(state, self.repair_state_current)
-        self.repair_state_current = state
+        base_probe = torch.gather(base, 1, gidx)
+        state, info = self.fit_repair(base_probe, dense, weights, tokens, route)
         corrected = K.repair_apply(base, state, cfg.repair_alpha, rows, dense)
-        info = {
-            "probe_rows": count,
-            "probe_selection_policy": cfg.probe_selection_policy,
-            "repair_rank": rank,
-            "repair_feature_dim": dim,
-            "repair_features": cfg.repair_features,
-            "repair_basis_source": cfg.repair_basis_source,
-            "repair_backend": "sparsepr_b200",
-            "repair_recovery_policy": policy,
-            "effective_video_density": _clamp_density(route.base_video_density + count / float(tokens)),
-        }
         return corrected.view(batch, heads, tokens, dim), info

@@ -40,6 +40,9 @@ def test_version_and_error_message(lib):
         _lib.call("spr_select_budget", None, None, None, 1, 1, 4096, None, None, None, None)
     with pytest.raises(RuntimeError, match="SPR_ERR_SHAPE.*d=128"):
         _lib.call("spr_block_sparse_attn", None, None, None, None, None, None, None, 1, 8, 8, 64, 1, 1, None, None,
+                  None, None, 0, None)
+    with pytest.raises(RuntimeError, match="SPR_ERR_SHAPE.*m=0"):
+        _lib.call("spr_probe_rows_attn", None, None, None, None, None, None, None, 1, 8, 8, 128, 1, 1, 0, None, None,
                   None, 0, None)
     with pytest.raises(RuntimeError, match="SPR_ERR_WORKSPACE"):
         _lib.call("spr_label_sort", None, 1, 100, 4, None, None, None, None, 0, None)

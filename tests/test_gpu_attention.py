@@ -224,7 +224,7 @@ def test_sparse_attention_matches_oracle_on_same_route(cuda):
     last-bit differences between eigensolvers)."""
     cfg = _cfg()
     q, k, v = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
-    out, density, info = sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg))
+    out, density, info = sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg), return_base=True)
     r = info["route"]
     _ref, _route, base_ref, (_state, rows_ref, _w, _dense) = oracle.oracle_sparse_attention(
         q, k, v, _oracle_cfg(cfg), route=_route_view(r, 2))
@@ -348,3 +348,44 @@ def test_hunyuan_layout_matches_oracle(cuda, prompt, pad):
     assert out.shape == q.shape and torch.isfinite(out.float()).all()
     assert torch.equal(out[:, :, n_video:], att.cpu()[:, :, n_video:])  # text rows: attended, not repaired
     assert not torch.equal(out[:, :, :n_video], att.cpu()[:, :, :n_video])  # video rows: repaired
+
+
+def test_probe_rows_pass_matches_oracle(cuda):
+    """The probe pre-pass: exact dense rows and the rows' sparse output (their
+    query cluster's kept key clusters) in one kernel, against the oracle."""
+    g = torch.Generator().manual_seed(77)
+    bh, n, cq, ck, m = 3, 3000, 17, 60, 40
+    q, k, v = (torch.randn(bh, n, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    qs, ks, mask = _random_layout(g, bh, n, cq, ck, 0.3)
+    qlab = torch.stack([torch.repeat_interleave(torch.arange(cq), qs[h]) for h in range(bh)])
+    order = torch.stack([torch.randperm(n, generator=g) for _ in range(bh)])  # original order of the sorted rows
+    q_orig = oracle.inverse_permute_rows(q, order)  # row order[s] of q_orig = sorted row s
+    lab_orig = torch.empty_like(qlab)
+    lab_orig.scatter_(1, order, qlab)
+    rows = torch.stack([torch.randperm(n, generator=g)[:m] for _ in range(bh)])
+    routed = torch.zeros(bh, cq + 1, ck + 1, dtype=torch.bool)
+    routed[:, 1:, 1:] = mask
+    dense, base = K.probe_rows_attention(q_orig.to(cuda), k.to(cuda), v.to(cuda), _i32(oracle.cluster_offsets(ks), cuda),
+                                         routed.to(cuda), _i32(rows, cuda), _i32(torch.gather(lab_orig, 1, rows), cuda))
+    torch.cuda.synchronize()
+    gi = rows.unsqueeze(2).expand(-1, -1, 128)
+    _close(dense, oracle.dense_attention_rows(torch.gather(q_orig, 1, gi), k, v))
+    ref_base = oracle.inverse_permute_rows(oracle.block_sparse_attention(q, k, v, mask, qs, ks), order)
+    _close(base, torch.gather(ref_base, 1, gi))
+
+
+def test_fused_repair_equals_attention_then_apply(cuda):
+    """The repair in the attention epilogue gives the same bits as storing the
+    attention output and running the standalone apply + probe overwrite."""
+    cfg = _cfg()
+    q, k, v = (t.to(cuda) for t in synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16))
+    core = N8V6Core(cfg)
+    out, _d, info = sparse_attention(q, k, v, core, return_base=True, fused_repair=True)
+    assert info["repair_fused"]
+    r = info["route"]
+    state = info["repair_state"]
+    ref = K.repair_apply(info["base"], state, cfg.repair_alpha, r.probe_rows, info["probe_dense"])
+    assert torch.equal(out.view(2, -1, 128), ref)
+    # The probe pre-pass's sparse rows agree with the attention output at those rows.
+    gi = r.probe_rows.long().unsqueeze(2).expand(-1, -1, 128)
+    _close(info["probe_base"], torch.gather(info["base"], 1, gi))

@@ -47,7 +47,7 @@ def test_production_layer_matches_oracle_on_build_route(cuda, config):
     grid = GRIDS[config]
     cfg = N8V6Config(**SETTINGS)
     q, k, v = synthetic_qkv_heads(0, 2, 128, grid, device=cuda)
-    out, density, info = sparse_attention(q, k, v, N8V6Core(cfg))
+    out, density, info = sparse_attention(q, k, v, N8V6Core(cfg), return_base=True)
     torch.cuda.synchronize()
     r = info["route"]
     bh, n = 2, q.shape[2]
