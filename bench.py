@@ -127,6 +127,36 @@ def _print_kernel_table(step, q, k, v, dev):
     print(f"{'total':72s} {'':6s} {total / 1e3:9.3f}")
 
 
+def _budget_modes(route, q, k, v, init_rows, cfg, dev, n):
+    """The reference's two budget modes (``n8_v6.py:1026-1061``) side by side: the
+    shipped fixed density (the timed bench line) and SVG top-p budgets (cumulative
+    softmax mass 0.3, the literal reading of "keep 30% of cluster-pair mass"), each
+    with its achieved cluster-pair density; the top-p layer is timed eagerly
+    (CUDA events, second of two calls).  A side measurement, not the bench value."""
+    from sparsepr_b200 import N8V6Config, N8V6Core, sparse_attention
+    from sparsepr_b200.attention import kept_flops
+
+    heads = q.shape[1]
+
+    def pair_density(rt):
+        pairs = (rt.video_dynamic_map.long() * rt.k_cluster_sizes.long().unsqueeze(1)).sum(-1)
+        return float((pairs * rt.q_cluster_sizes.long()).sum().item()) / float(heads * n * n)
+
+    modes = {"fixed_density": {"target_density": SPARSE["target_density"], "pair_density": pair_density(route)}}
+    cfg_tp = N8V6Config(**{**SPARSE, "selector_budget_mode": "svg_ear_top_p", "svg_ear_top_p": 0.3})
+    for _ in range(2):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _out, dens, info = sparse_attention(q, k, v, N8V6Core(cfg_tp, init_indices=init_rows))
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    kept = int(kept_flops(info["route"], 128, cfg.probe_rows, n).item())
+    modes["svg_ear_top_p"] = {"top_p": 0.3, "pair_density": pair_density(info["route"]), "reported_density": dens,
+                              "ms_eager": ms, "kept_tflops": kept / (ms * 1e-3) / 1e12}
+    return modes
+
+
 def _print_route_reuse(cfg, q, k, v, dev, args):
     """Device time of a refreshed layer call and of a temporal-reuse call
     (cached route, current Q/K/V) through ``RouteCache``; one JSON line.
@@ -196,7 +226,7 @@ def run_b200(args):
     route = info["route"]
     sel_keys = (route.video_dynamic_map.long() * route.k_cluster_sizes.long().unsqueeze(1)).sum(-1)
     attn_flops = int((4 * 128 * (sel_keys * route.q_cluster_sizes.long()).sum()).item())
-    del out, info, route
+    del out, info
 
     if args.kernel_table:
         _print_kernel_table(step, q, k, v, dev)
@@ -204,6 +234,9 @@ def run_b200(args):
     if args.route_reuse:
         _print_route_reuse(cfg, q, k, v, dev, args)
         return
+    # Both budget modes of the reference, each with its achieved pair density (N = 1 only).
+    budget_modes = _budget_modes(route, q, k, v, init_rows, cfg, dev, n) if world == 1 else None
+    del route
 
     # Eager pass: per-kernel events for the attention roofline and the launch count.
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -302,6 +335,7 @@ def run_b200(args):
                          "attn_ms": attn_ms,
                          "attn_share_of_step": attn_ms / ms},
             "gpu_launches": int(launches),
+            "budget_modes": budget_modes,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -389,3 +389,37 @@ def test_fused_repair_equals_attention_then_apply(cuda):
     # The probe pre-pass's sparse rows agree with the attention output at those rows.
     gi = r.probe_rows.long().unsqueeze(2).expand(-1, -1, 128)
     _close(info["probe_base"], torch.gather(info["base"], 1, gi))
+
+
+def test_top_p_budgets_route_and_layer_match_oracle(cuda):
+    """selector_budget_mode="svg_ear_top_p" (n8_v6.py:1041-1061, 181-230): the
+    per-query-cluster key budgets from the build's centroids against the
+    oracle's restatement (>= 95% identical: a cumulative-mass cutoff can move by
+    one cluster on fp32 rounding), the map bit-exact given the scores and the
+    budgets, the layer on that route against the oracle, and the device-side
+    density the graph path reports."""
+    from sparsepr_b200.graph import GraphedSparseAttention
+
+    cfg = _cfg(selector_budget_mode="svg_ear_top_p", svg_ear_top_p=0.3)
+    q, k, v = synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16)
+    out, density, info = sparse_attention(q.to(cuda), k.to(cuda), v.to(cuda), N8V6Core(cfg), return_base=True)
+    r = info["route"]
+    q3, k3, v3 = (t.view(2, -1, 128) for t in (q, k, v))
+    ql, kl = r.q_labels.cpu().long(), r.k_labels.cpu().long()
+    qs, ks = r.q_cluster_sizes.cpu().long(), r.k_cluster_sizes.cpu().long()
+    qcent = oracle.original_centroids(q3, ql, qs)
+    kcent = oracle.original_centroids(k3, kl, ks)
+    ref_b = oracle.svg_top_p_key_budgets(qcent, kcent, ks, 0.3)
+    got_b = r.budgets.cpu().long()
+    assert (got_b == ref_b).float().mean().item() >= 0.95
+    routed = oracle.select_budget(r.scores.cpu(), ks, got_b)
+    assert torch.equal(r.video_dynamic_map.cpu(), routed[:, 1:, 1:])
+    _ref, _r, base_ref, _extra = oracle.oracle_sparse_attention(q, k, v, _oracle_cfg(cfg), route=_route_view(r, 2))
+    _close(info["base"].cpu(), base_ref)
+    pair = oracle.kept_pairs(r.video_dynamic_map.cpu(), qs, ks) / float(2 * q.shape[2] ** 2)
+    assert 0.0 < pair < 1.0 and 0.0 < density <= 1.0
+    g = GraphedSparseAttention(q.shape, cfg, cuda).capture()
+    got = g(q.to(cuda), k.to(cuda), v.to(cuda)).clone()
+    torch.cuda.synchronize()
+    assert isinstance(g.density, torch.Tensor) and abs(float(g.density) - density) < 1e-6
+    _close(got.view(2, -1, 128), out.view(2, -1, 128))

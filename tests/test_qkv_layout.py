@@ -98,3 +98,49 @@ def test_install_hunyuan_patch_replaces_the_processor_method():
     old = Processor._sparse_attention
     prev = A.install_hunyuan_sparse_patch(Processor)
     assert prev is old and Processor._sparse_attention is not old
+
+
+def _reference_src():
+    """The reference checkout's src/ next to this repository, when present (it is
+    only in the build container, never on a GPU box)."""
+    import os
+
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = os.path.join(os.path.dirname(here), "reference", "src")
+    return src if os.path.isdir(os.path.join(src, "sparsepr", "adapters")) else None
+
+
+def test_install_into_the_real_reference_adapter():
+    """The patch installed into the reference's own sparsepr.adapters.wan22: its
+    _sparse_n8_attention (wan22.py:1926-1942) then runs this build's body
+    (BLHD -> BHLD conversion by the reference, routing here), and its core
+    factory builds this build's N8V6Core.  On the CPU the build's routing
+    refuses the call, which proves the call reached it."""
+    import importlib
+    import sys
+    import types
+
+    src = _reference_src()
+    if src is None:
+        pytest.skip("reference sources not present")
+    sys.path.insert(0, src)
+    try:
+        wan22 = importlib.import_module("sparsepr.adapters.wan22")
+    except Exception as e:  # an optional dependency of the adapter module is missing
+        pytest.skip(f"reference adapter does not import here: {e!r}")
+    finally:
+        sys.path.remove(src)
+    from sparsepr_b200 import N8V6Core
+    from sparsepr_b200 import attention as A
+
+    prev = A.install_wan22_ti2v_sparse_patch(module=wan22)
+    try:
+        assert wan22._sparse_n8_attention_bhld is A.sparse_n8_attention_bhld
+        assert isinstance(wan22._make_n8_core(), N8V6Core)
+        attn = types.SimpleNamespace()
+        q = torch.randn(1, 64, 2, 128)  # [B, L, H, D] as the Wan attention passes it
+        with pytest.raises(RuntimeError, match="sparsepr_b200 N8-V6 routing runs on CUDA tensors only"):
+            wan22._sparse_n8_attention(attn, q, q, q, None)
+        assert isinstance(attn._n8_cores[0], N8V6Core)  # the branch-local core cache of wan22.py:1551-1566
+    finally:
+        wan22._sparse_n8_attention_bhld, wan22._make_n8_core = prev
