@@ -20,7 +20,7 @@ __all__ = ["sparse_attention", "hunyuan_sparse_attention", "hunyuan_attend", "in
 
 
 def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, attn_events=None,
-                     return_base: bool = False, fused_repair: bool = False, **route_kw):
+                     return_base: bool = False, fused_repair: bool = True, **route_kw):
     """One SparsePR attention call on [B,H,N,D] Q/K/V.
 
     Returns ``(repaired [B,H,N,D] bf16, density float, info dict)`` like the
@@ -30,13 +30,13 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     ``repair_state``; ``attn_events`` (optional pair of ``torch.cuda.Event``)
     brackets the block-sparse attention launch on the current stream.
 
-    With ``fused_repair=True`` the repair runs fused into the attention
-    epilogue where the configuration allows it
-    (``N8V6Core.fused_repair_supported``): a probe pre-pass computes the probe
-    rows' exact and sparse outputs in one kernel, the state is fitted from
-    them, and the attention kernel applies it and overwrites the probe rows
-    before its store.  Otherwise the attention output is stored and
-    ``N8V6Core.repair`` applies the repair.
+    The repair runs fused into the attention epilogue where the configuration
+    allows it (``N8V6Core.fused_repair_supported``): a probe pre-pass computes
+    the probe rows' exact and sparse outputs in one kernel, the state is
+    fitted from them, and the attention kernel applies it (the rank-16
+    correction on the tensor cores) and overwrites the probe rows before its
+    store.  Otherwise, or with ``fused_repair=False``, the attention output is
+    stored and ``N8V6Core.repair`` applies the repair.
     ``return_base`` also returns the unrepaired output as ``info["base"]``
     (an extra attention launch on the fused path; for tests).
     """

@@ -69,14 +69,20 @@ constexpr int kMaxProbes = 128;
 enum : int { kModePlain = 0, kModeRepair = 1, kModeProbe = 2 };
 
 // Fused repair state (kModeRepair), per problem b:
-//   lfold [b][128][16] = L / x_scale, c0 [b][16] = -sum_d x_mean[d] lfold[d][:],
-//   basis [b][128][16], y_mean [b][128]; probe_tok [b][m] ascending token ids
-//   and probe_dense [b][m][128] their exact rows.
-// out = bf16(v + alpha * (y_mean + (v lfold + c0) basis^T)), v = bf16(attention row).
+//   image [b] (kRepairImageBytes): the tensor-core operands of the correction,
+//     laid out as their shared-memory tiles (128-byte swizzle, K-major), each
+//     fp32 matrix as a bf16 (hi, lo) pair, hi + lo = the value to ~2^-16:
+//       L'hi, L'lo  [16 rows j][128 K d]  (L' = L / x_scale)        4 KB each
+//       Bhi, Blo    [128 rows d][64 K j, j < 16 used, rest 0]       16 KB each
+//   c0 [b][16] = -sum_d x_mean[d] L'[d][:], y_mean [b][128];
+//   probe_tok [b][m] ascending token ids and probe_dense [b][m][128] their exact rows.
+// out = bf16(v + alpha * (y_mean + (v L' + c0) B^T)), v = bf16(attention row).
+constexpr int kImgL = 16 * kD * 2;        // one L' part
+constexpr int kImgB = kD * 128;           // one B part (128 rows x 128 bytes)
+constexpr int kRepairImageBytes = 2 * kImgL + 2 * kImgB;
 struct AttnRepair {
-  const float* lfold;
+  const uint8_t* image;
   const float* c0;
-  const float* basis;
   const float* y_mean;
   const int32_t* probe_tok;
   const __nv_bfloat16* probe_dense;
@@ -103,6 +109,7 @@ constexpr int kTileBytes = kTileM * kD * 2;    // 32 KB per 128 x 128 bf16 tile
 constexpr int kSmemTc = 1024 /*align slack*/ + 2 * kTileBytes /*Q_A, Q_B*/ + 4 * kTileBytes /*K,V x2*/;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, 0);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 1);
+constexpr uint32_t kIdescD1 = idesc_bf16_f32(128, 16, 0);  // repair: v L' (N = 16, both K-major)
 
 enum : int { kErrTimeoutLoad = 1, kErrTimeoutMma = 2, kErrTimeoutSoftmax = 3 };
 
@@ -185,11 +192,12 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   __shared__ int32_t s_run_start[kRuns];
   __shared__ int32_t s_run_end[kRuns + 1];  // inclusive prefix of run lengths
   __shared__ int s_total;
-  // Fused repair weights (kModeRepair only; one element otherwise).
-  constexpr int kRW = MODE == kModeRepair ? kD * kRepairRank : 1;
-  __shared__ __align__(16) float s_lf[kRW], s_bs[kRW];
+  // Fused repair (kModeRepair only; one element otherwise).
   __shared__ float s_c0[MODE == kModeRepair ? kRepairRank : 1], s_ym[MODE == kModeRepair ? kD : 1];
   __shared__ int32_t s_ptok[MODE == kModeRepair ? kMaxProbes : 1];
+  // Epilogue barriers of the repair MMAs (single phase): operand image landed,
+  // rows v of tile x written, D1 = v L' done, coords of tile x written, D2 done.
+  __shared__ uint64_t bar_img, bar_v_ready[2], bar_d1[2], bar_a2_ready[2], bar_d2[2];
 
   const int64_t b = blockIdx.y;
   int c = 0, row0 = 0, rows_a, rows_b;
@@ -239,11 +247,16 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
     mbar_fence_init();
   }
   if (warp == 8) tmem_alloc<512>(&s_tmem);
-  if constexpr (MODE == kModeRepair) {  // repair weights and probe tokens of this problem
-    const int64_t wo = b * (int64_t)(kD * kRepairRank);
-    for (int i = tid; i < kD * kRepairRank; i += kThreadsTc) {
-      s_lf[i] = rep.lfold[wo + i];
-      s_bs[i] = rep.basis[wo + i];
+  if constexpr (MODE == kModeRepair) {  // repair vectors and probe tokens of this problem
+    if (tid == 0) {
+      mbar_init(&bar_img, 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&bar_v_ready[i], kSoftmaxThreads);
+        mbar_init(&bar_d1[i], 1);
+        mbar_init(&bar_a2_ready[i], kSoftmaxThreads);
+        mbar_init(&bar_d2[i], 1);
+      }
+      mbar_fence_init();
     }
     if (tid < kRepairRank) s_c0[tid] = rep.c0[b * kRepairRank + tid];
     if (tid < kD) s_ym[tid] = rep.y_mean[b * kD + tid];
@@ -400,6 +413,60 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       }
       mma_commit(&bar_o_done[0]);
       mma_commit(&bar_o_done[1]);
+    }
+    if constexpr (MODE == kModeRepair) {
+      // Repair MMAs of the epilogue, per query tile x: D1 = v L' (two bf16 parts
+      // of L', N = 16) into the first columns of x's O region, then
+      // D2 = coords B^T (hi.hi + hi.lo + lo.hi, one K = 16 step each) into x's
+      // S region.  The operand image goes to the K/V rings, free once every
+      // MMA above has completed.
+      if (lane == 0) {
+        bool eok = true;
+        if (ntiles > 0)
+          eok = mbar_wait(&bar_o_done[0], 0, err, kErrTimeoutMma) && mbar_wait(&bar_o_done[1], 0, err, kErrTimeoutMma);
+        const uint32_t img = smem_addr(sK);
+        const uint32_t l_hi = img, l_lo = img + kImgL, b_hi = img + 2 * kImgL, b_lo = b_hi + kImgB;
+        const uint32_t a2 = img + kRepairImageBytes;  // [tile][hi, lo] coords tiles, 128 rows x 128 B each
+        bool img_issued = false;
+        if (eok) {
+          tc_fence_after();
+          mbar_expect_tx(&bar_img, (uint32_t)kRepairImageBytes);
+          bulk_load(img, rep.image + b * (int64_t)kRepairImageBytes, (uint32_t)kRepairImageBytes, &bar_img);
+          img_issued = true;
+          eok = mbar_wait(&bar_img, 0, err, kErrTimeoutMma);
+        }
+        const int tiles = has_b ? 2 : 1;
+        for (int xt = 0; eok && xt < tiles; ++xt) {
+          if (!(eok = mbar_wait(&bar_v_ready[xt], 0, err, kErrTimeoutMma))) break;
+          tc_fence_after();
+          const uint32_t va = smem_addr(sQ + xt * kTileBytes);
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t koff_a = (kk >> 2) * (kTileM * 128) + (kk & 3) * 32;
+              const uint32_t koff_b = (kk >> 2) * (16 * 128) + (kk & 3) * 32;
+              mma_f16(tmem + 256 * xt + 128, sw128_desc(va + koff_a, 16, 1024),
+                      sw128_desc((part ? l_lo : l_hi) + koff_b, 16, 1024), kIdescD1, (part > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&bar_d1[xt]);
+        }
+        for (int xt = 0; eok && xt < tiles; ++xt) {
+          if (!(eok = mbar_wait(&bar_a2_ready[xt], 0, err, kErrTimeoutMma))) break;
+          tc_fence_after();
+          const uint32_t a_hi = a2 + xt * 2 * kImgB, a_lo = a_hi + kImgB;
+          mma_f16(tmem + 256 * xt, sw128_desc(a_hi, 16, 1024), sw128_desc(b_hi, 16, 1024), kIdescQK, 0u);
+          mma_f16(tmem + 256 * xt, sw128_desc(a_hi, 16, 1024), sw128_desc(b_lo, 16, 1024), kIdescQK, 1u);
+          mma_f16(tmem + 256 * xt, sw128_desc(a_lo, 16, 1024), sw128_desc(b_hi, 16, 1024), kIdescQK, 1u);
+          mma_commit(&bar_d2[xt]);
+        }
+        // Every MMA issued here has finished before TMEM is freed; a copy still
+        // in flight (a wait gave up) lands before the CTA exits.
+        mma_commit(&bar_o_done[0]);
+        if (img_issued) mbar_drain(&bar_img, 0);
+        mbar_drain(&bar_o_done[0], ntiles > 0 ? 1 : 0);
+      }
     }
   } else if (warp < 4 || has_b) {
     // ------------------------------------------------------------ softmax (thread = row)
@@ -562,16 +629,13 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
         prb.ml_part[2 * pr + 1] = any ? l_run : 0.f;
       }
     } else if constexpr (MODE == kModeRepair) {
-      // v = bf16(O / l); coords = v L' + c0 (first pass over O); then
-      // out = bf16(v + alpha (y_mean + coords B^T)) (second pass), or the
-      // exact dense row for a probe token.  Same operation order as the
-      // standalone repair apply, so the result equals attention-then-apply.
+      // v = bf16(O / l) into x's Q tile (K-major, the MMA layout); the MMA
+      // warp forms D1 = v L'; coords = D1 + c0 go back as bf16 (hi, lo) rows;
+      // the MMA warp forms D2 = coords B^T; out = bf16(v + alpha (y_mean + D2)),
+      // or the exact dense row for a probe token.
       const int64_t s_row = row0 + x * kTileM + row;
       const int64_t dst = (row < rows) ? (q_order ? (int64_t)q_order[b * nq + s_row] : s_row) : 0;
-      // coords as packed pairs (j, j+1); each lane of an f32x2 FMA rounds like fmaf.
-      unsigned long long cp2[kRepairRank / 2];
-#pragma unroll
-      for (int jr = 0; jr < kRepairRank / 2; ++jr) cp2[jr] = pk2(s_c0[2 * jr], s_c0[2 * jr + 1]);
+      uint8_t* vt = sQ + x * kTileBytes;
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         float o[32];
@@ -582,26 +646,52 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
           for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float vv = __bfloat162float(__float2bfloat16_rn(o[i] * inv));
-          const unsigned long long vv2 = pk2(vv, vv);
-          const float4* lf = reinterpret_cast<const float4*>(s_lf + (cb * 32 + i) * kRepairRank);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
 #pragma unroll
-          for (int q4 = 0; q4 < kRepairRank / 4; ++q4) {
-            const float4 l4 = lf[q4];
-            cp2[2 * q4] = fma2(vv2, pk2(l4.x, l4.y), cp2[2 * q4]);
-            cp2[2 * q4 + 1] = fma2(vv2, pk2(l4.z, l4.w), cp2[2 * q4 + 1]);
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 hh = __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv, o[q4 * 8 + 2 * e + 1] * inv);
+            w[e] = *reinterpret_cast<uint32_t*>(&hh);
           }
+          *reinterpret_cast<uint4*>(vt + sw128_off(row, cb * 4 + q4, kTileM)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      unsigned long long cc2[kRepairRank];  // (coord_j, coord_j) for the second pass
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_v_ready[x]);
+      bool eok = __all_sync(0xffffffffu, mbar_wait(&bar_d1[x], 0, err, kErrTimeoutSoftmax));
+      tc_fence_after();
+      {
+        float d1v[32];
+        if (eok) {
+          tmem_ld32(tO, d1v);  // columns 0..15 hold D1
+        } else {
 #pragma unroll
-      for (int jr = 0; jr < kRepairRank / 2; ++jr) {
-        float c_lo, c_hi;
-        up2(cp2[jr], c_lo, c_hi);
-        cc2[2 * jr] = pk2(c_lo, c_lo);
-        cc2[2 * jr + 1] = pk2(c_hi, c_hi);
+          for (int i = 0; i < 32; ++i) d1v[i] = 0.f;
+        }
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int jp = 0; jp < kRepairRank / 2; ++jp) {
+          const float c0v = d1v[2 * jp] + s_c0[2 * jp], c1v = d1v[2 * jp + 1] + s_c0[2 * jp + 1];
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(c0v, c1v);
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(c0v - __low2float(hi), c1v - __high2float(hi));
+          hw[jp] = *reinterpret_cast<const uint32_t*>(&hi);
+          lw[jp] = *reinterpret_cast<const uint32_t*>(&lo);
+        }
+        uint8_t* a2 = sK + kRepairImageBytes + x * 2 * kImgB;  // coords tiles of this query tile
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          *reinterpret_cast<uint4*>(a2 + sw128_off(row, ch, kTileM)) =
+              make_uint4(hw[4 * ch], hw[4 * ch + 1], hw[4 * ch + 2], hw[4 * ch + 3]);
+          *reinterpret_cast<uint4*>(a2 + kImgB + sw128_off(row, ch, kTileM)) =
+              make_uint4(lw[4 * ch], lw[4 * ch + 1], lw[4 * ch + 2], lw[4 * ch + 3]);
+        }
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar_a2_ready[x]);
+      eok = eok && __all_sync(0xffffffffu, mbar_wait(&bar_d2[x], 0, err, kErrTimeoutSoftmax));
+      tc_fence_after();
       // Probe token?  (s_ptok ascending; -1 when not found.)
       int probe = -1;
       {
@@ -617,12 +707,12 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
       const uint4* prow = reinterpret_cast<const uint4*>(rep.probe_dense + (b * rep.m + max(probe, 0)) * (int64_t)kD);
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
-        float o[32];
-        if (have) {
-          tmem_ld32(tO + cb * 32, o);
+        float d2v[32];
+        if (eok) {
+          tmem_ld32(tS + cb * 32, d2v);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          for (int i = 0; i < 32; ++i) d2v[i] = 0.f;
         }
         if (row < rows) {
 #pragma unroll
@@ -631,27 +721,16 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
             if (probe >= 0) {
               w4 = prow[cb * 4 + q4];
             } else {
+              const uint4 vv = *reinterpret_cast<const uint4*>(vt + sw128_off(row, cb * 4 + q4, kTileM));
+              const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
               uint32_t w[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                // Output columns d, d+1 as one packed pair: y_mean + sum_j coord_j B[.][j] in j order.
+                const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(&vw[e]);
                 const int dcol = cb * 32 + q4 * 8 + 2 * e;
-                const float4* bs0 = reinterpret_cast<const float4*>(s_bs + dcol * kRepairRank);
-                const float4* bs1 = reinterpret_cast<const float4*>(s_bs + (dcol + 1) * kRepairRank);
-                unsigned long long acc2 = pk2(s_ym[dcol], s_ym[dcol + 1]);
-#pragma unroll
-                for (int q = 0; q < kRepairRank / 4; ++q) {
-                  const float4 b0 = bs0[q], b1 = bs1[q];
-                  acc2 = fma2(cc2[4 * q], pk2(b0.x, b1.x), acc2);
-                  acc2 = fma2(cc2[4 * q + 1], pk2(b0.y, b1.y), acc2);
-                  acc2 = fma2(cc2[4 * q + 2], pk2(b0.z, b1.z), acc2);
-                  acc2 = fma2(cc2[4 * q + 3], pk2(b0.w, b1.w), acc2);
-                }
-                const float v0 = __bfloat162float(__float2bfloat16_rn(o[q4 * 8 + 2 * e] * inv));
-                const float v1 = __bfloat162float(__float2bfloat16_rn(o[q4 * 8 + 2 * e + 1] * inv));
-                float a0, a1;
-                up2(fma2(pk2(rep.alpha, rep.alpha), acc2, pk2(v0, v1)), a0, a1);
-                __nv_bfloat162 hh = __floats2bfloat162_rn(a0, a1);
+                const float r0 = fmaf(rep.alpha, s_ym[dcol] + d2v[q4 * 8 + 2 * e], __low2float(v2));
+                const float r1 = fmaf(rep.alpha, s_ym[dcol + 1] + d2v[q4 * 8 + 2 * e + 1], __high2float(v2));
+                __nv_bfloat162 hh = __floats2bfloat162_rn(r0, r1);
                 w[e] = *reinterpret_cast<uint32_t*>(&hh);
               }
               w4 = make_uint4(w[0], w[1], w[2], w[3]);
@@ -700,16 +779,36 @@ block_sparse_attn_tc_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
 
 namespace spr {
 
-// Fold the standardisation into the left factor: lfold[b][d][j] = L[b][d][j] / xs[b][d]
-// (correctly rounded division) and c0[b][j] = -sum_d xm[b][d] lfold[b][d][j] in d order.
+// Per problem b: L' = L / xs (correctly rounded division), c0[j] = -sum_d xm[d] L'[d][j]
+// in d order, and the repair operand image of the attention epilogue (bf16 hi/lo
+// parts of L'^T [16 x 128] and of B [128 x 16] in their 128-byte-swizzled
+// K-major shared-memory layouts, B's K padded with zeros to 64).
 __global__ void repair_fold_kernel(const float* __restrict__ xm, const float* __restrict__ xs,
-                                   const float* __restrict__ left, float* __restrict__ lfold, float* __restrict__ c0) {
+                                   const float* __restrict__ left, const float* __restrict__ basis,
+                                   uint8_t* __restrict__ image, float* __restrict__ c0) {
   const int64_t b = blockIdx.x;
   __shared__ float sh[kD * kRepairRank];
+  uint8_t* img = image + b * (int64_t)kRepairImageBytes;
   for (int i = threadIdx.x; i < kD * kRepairRank; i += blockDim.x) {
-    const float v = __fdiv_rn(left[b * kD * kRepairRank + i], xs[b * kD + i / kRepairRank]);
-    sh[i] = v;
-    lfold[b * kD * kRepairRank + i] = v;
+    const int d = i / kRepairRank, j = i % kRepairRank;
+    const float lv = __fdiv_rn(left[b * kD * kRepairRank + i], xs[b * kD + d]);
+    sh[i] = lv;
+    // L'^T: row j, K index d.
+    const __nv_bfloat16 lh = __float2bfloat16_rn(lv);
+    const __nv_bfloat16 ll = __float2bfloat16_rn(lv - __bfloat162float(lh));
+    const uint32_t lo = sw128_off(j, d >> 3, 16) + (d & 7) * 2;
+    *reinterpret_cast<__nv_bfloat16*>(img + lo) = lh;
+    *reinterpret_cast<__nv_bfloat16*>(img + kImgL + lo) = ll;
+  }
+  for (int i = threadIdx.x; i < kD * 64; i += blockDim.x) {
+    // B: row d, K index j (j >= 16 is zero padding).
+    const int d = i / 64, j = i % 64;
+    const float bv = j < kRepairRank ? basis[b * kD * kRepairRank + d * kRepairRank + j] : 0.f;
+    const __nv_bfloat16 bh = __float2bfloat16_rn(bv);
+    const __nv_bfloat16 bl = __float2bfloat16_rn(bv - __bfloat162float(bh));
+    const uint32_t bo = sw128_off(d, j >> 3, kD) + (j & 7) * 2;
+    *reinterpret_cast<__nv_bfloat16*>(img + 2 * kImgL + bo) = bh;
+    *reinterpret_cast<__nv_bfloat16*>(img + 2 * kImgL + kImgB + bo) = bl;
   }
   __syncthreads();
   if (threadIdx.x < kRepairRank) {
@@ -763,7 +862,7 @@ static int launch_attn(dim3 grid, const void* q, const void* k, const void* v, c
 
 using namespace spr;
 
-static size_t repair_fold_floats(int64_t bh) { return (size_t)bh * (kD * kRepairRank + kRepairRank); }
+static size_t repair_fold_floats(int64_t bh) { return (size_t)bh * (kRepairImageBytes / 4 + kRepairRank); }
 
 extern "C" size_t spr_block_sparse_attn_workspace_bytes(int64_t bh, int64_t nq, int cq) {
   (void)nq;
@@ -813,13 +912,13 @@ extern "C" int spr_block_sparse_attn(const void* q_perm, const void* k_perm, con
   if (!repair)
     return launch_attn<kModePlain>(grid, q_perm, k_perm, v_perm, q_offsets, k_offsets, sel_ids, sel_counts,
                                    tile_start, nq, nk, d, cq, ck, q_order, out, err, rep, prb, st);
-  float* lfold = fold;
-  float* c0 = fold + (size_t)bh * kD * kRepairRank;
-  repair_fold_kernel<<<(unsigned)bh, 256, 0, st>>>(repair->x_mean, repair->x_scale, repair->left, lfold, c0);
+  uint8_t* image = reinterpret_cast<uint8_t*>(fold);
+  float* c0 = fold + (size_t)bh * (kRepairImageBytes / 4);
+  repair_fold_kernel<<<(unsigned)bh, 256, 0, st>>>(repair->x_mean, repair->x_scale, repair->left, repair->basis,
+                                                   image, c0);
   if ((s = check_launch("fused repair: fold"))) return s;
-  rep.lfold = lfold;
+  rep.image = image;
   rep.c0 = c0;
-  rep.basis = repair->basis;
   rep.y_mean = repair->y_mean;
   rep.probe_tok = repair->probe_rows;
   rep.probe_dense = (const __nv_bfloat16*)repair->probe_dense;

@@ -375,8 +375,8 @@ def test_probe_rows_pass_matches_oracle(cuda):
 
 
 def test_fused_repair_equals_attention_then_apply(cuda):
-    """The repair in the attention epilogue gives the same bits as storing the
-    attention output and running the standalone apply + probe overwrite."""
+    """The repair in the attention epilogue equals storing the attention output
+    and running the standalone apply + probe overwrite (to bf16 rounding)."""
     cfg = _cfg()
     q, k, v = (t.to(cuda) for t in synthetic_qkv(2, 128, (4, 8, 16), dtype=torch.bfloat16))
     core = N8V6Core(cfg)
@@ -385,7 +385,14 @@ def test_fused_repair_equals_attention_then_apply(cuda):
     r = info["route"]
     state = info["repair_state"]
     ref = K.repair_apply(info["base"], state, cfg.repair_alpha, r.probe_rows, info["probe_dense"])
-    assert torch.equal(out.view(2, -1, 128), ref)
+    # The epilogue forms the rank-16 correction on the tensor cores from bf16
+    # (hi, lo) operand pairs (~2^-16 relative), the apply kernel with fp32 FMAs:
+    # the same bf16 result up to rounding-boundary cases.
+    got = out.view(2, -1, 128)
+    assert (got == ref).float().mean().item() >= 0.97
+    _close(got, ref)
+    diff = (got.float() - ref.float()).abs()
+    assert (diff <= ref.float().abs() * 2 ** -7 + 2e-3).all(), diff.max().item()
     # The probe pre-pass's sparse rows agree with the attention output at those rows.
     gi = r.probe_rows.long().unsqueeze(2).expand(-1, -1, 128)
     _close(info["probe_base"], torch.gather(info["base"], 1, gi))
