@@ -348,3 +348,4 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
       return fail(SPR_ERR_SHAPE, "sym_eig: n=%d not compiled (2,4,8,16,32,48,64,96,128)", n);
   }
 }
+

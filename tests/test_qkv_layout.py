@@ -144,3 +144,50 @@ def test_install_into_the_real_reference_adapter():
         assert isinstance(attn._n8_cores[0], N8V6Core)  # the branch-local core cache of wan22.py:1551-1566
     finally:
         wan22._sparse_n8_attention_bhld, wan22._make_n8_core = prev
+
+
+def _wan_fixture():
+    import os
+    import sys
+
+    golden = os.path.join(os.path.dirname(__file__), "golden")
+    sys.path.insert(0, golden)
+    try:
+        from make_wan_qkv_golden import cases, inputs
+    finally:
+        sys.path.remove(golden)
+    fx = torch.load(os.path.join(golden, "wan_qkv_layout_ref.pt"))
+    return cases(), inputs, fx["cases"]
+
+
+def _check_against_reference(got, want, dtype):
+    assert torch.equal(got[2], want[2])  # V: layout only
+    for o, r in zip(got[:2], want[:2]):
+        assert o.shape == r.shape and o.dtype == r.dtype
+        # The reference is built with fast math (approximate rsqrt); values may
+        # sit one rounding step apart.
+        same = (o == r).float().mean().item()
+        assert same > (0.98 if dtype != torch.float32 else 0.0), same
+        eps = {torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10, torch.float32: 1e-6}[dtype]
+        torch.testing.assert_close(o.float(), r.float(), rtol=2 * eps, atol=2 * eps)
+
+
+def test_oracle_matches_reference_kernel_outputs():
+    """The oracle restatement against the reference's own CUDA kernel's outputs
+    (tests/golden/wan_qkv_layout_ref.pt, make_wan_qkv_golden.py)."""
+    specs, make_inputs, recs = _wan_fixture()
+    for (dtype, b, l, h, hd), rec in zip(specs, recs):
+        args = make_inputs(dtype, b, l, h, hd, rec["seed"])
+        got = oracle.wan_qkv_norm_rope_layout(*args, heads=h, epsilon=rec["epsilon"])
+        _check_against_reference(got, rec["outputs"], dtype)
+
+
+@pytest.mark.gpu
+def test_kernel_matches_reference_kernel_outputs(cuda):
+    from sparsepr_b200 import kernels as K
+
+    specs, make_inputs, recs = _wan_fixture()
+    for (dtype, b, l, h, hd), rec in zip(specs, recs):
+        args = make_inputs(dtype, b, l, h, hd, rec["seed"])
+        got = K.wan_qkv_norm_rope_layout(*(t.to(cuda) for t in args), heads=h, epsilon=rec["epsilon"])
+        _check_against_reference([t.cpu() for t in got], rec["outputs"], dtype)
