@@ -15,7 +15,7 @@ import torch
 from . import kernels as K
 from .n8_v6 import N8V6Config, N8V6Core
 
-__all__ = ["sparse_attention", "hunyuan_sparse_attention", "hunyuan_attend", "install_hunyuan_sparse_patch", "Wan22TI2VSparseConfig", "install_wan22_ti2v_sparse_patch", "make_n8_core",
+__all__ = ["sparse_attention", "route_phase", "attend_phase", "hunyuan_sparse_attention", "hunyuan_attend", "install_hunyuan_sparse_patch", "Wan22TI2VSparseConfig", "install_wan22_ti2v_sparse_patch", "make_n8_core",
            "kept_flops", "sparse_n8_attention_bhld"]
 
 
@@ -40,6 +40,14 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
     ``return_base`` also returns the unrepaired output as ``info["base"]``
     (an extra attention launch on the fused path; for tests).
     """
+    route = route_phase(q, k, v, core, total_key_tokens=total_key_tokens, **route_kw)
+    return attend_phase(q, k, v, core, route, attn_events=attn_events, return_base=return_base,
+                        fused_repair=fused_repair)
+
+
+def route_phase(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = None, **route_kw):
+    """The routing half of :func:`sparse_attention` (checks, the previous
+    layer's status words, ``core.route``); returns the route."""
     if q.ndim != 4:
         raise RuntimeError(f"sparse_attention expects [B,H,N,D] tensors, got {tuple(q.shape)}.")
     batch, heads, tokens, dim = q.shape
@@ -47,8 +55,16 @@ def sparse_attention(q, k, v, core: N8V6Core, *, total_key_tokens: int | None = 
         raise RuntimeError("Wan2.2 N8 currently requires batch size one.")
     if q.is_cuda:
         K.raise_device_status(q.device)  # the previous layer's status words, if they have landed
-    route = core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
-                       **route_kw)
+    return core.route(q, k, v, total_key_tokens=tokens if total_key_tokens is None else total_key_tokens,
+                      **route_kw)
+
+
+def attend_phase(q, k, v, core: N8V6Core, route, *, attn_events=None, return_base: bool = False,
+                 fused_repair: bool = True):
+    """The attention half of :func:`sparse_attention` on a route from
+    :func:`route_phase`: probe pre-pass, fit, block-sparse attention with the
+    fused repair (or attention then ``core.repair``)."""
+    batch, heads, tokens, dim = q.shape
     bh = batch * heads
     k_perm, v_perm = route.k_permuted.view(bh, -1, dim), route.v_permuted.view(bh, -1, dim)
     base = None

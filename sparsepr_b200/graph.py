@@ -19,7 +19,7 @@ from .attention import sparse_attention
 from .n8_v6 import N8V6Config, N8V6Core
 from .synthetic import random_init_indices
 
-__all__ = ["GraphedSparseAttention", "StreamedSparseAttention"]
+__all__ = ["GraphedSparseAttention", "StreamedSparseAttention", "ConcurrentSparseAttention"]
 
 _SCOPE_IDS = itertools.count()
 
@@ -35,12 +35,21 @@ class GraphedSparseAttention:
     streams.
     """
 
-    def __init__(self, shape, config: N8V6Config, device: torch.device, warmup: int = 2):
+    def __init__(self, shape, config: N8V6Config, device: torch.device, warmup: int = 2, inputs=None):
+        """``inputs`` (optional): three device bf16 tensors of ``shape`` to use as
+        the static input buffers instead of private ones (e.g. views of a larger
+        buffer shared by several graphs)."""
         self.config = config
         self.device = device
-        self.q = torch.zeros(shape, dtype=torch.bfloat16, device=device)
-        self.k = torch.zeros_like(self.q)
-        self.v = torch.zeros_like(self.q)
+        if inputs is None:
+            self.q = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+            self.k = torch.zeros_like(self.q)
+            self.v = torch.zeros_like(self.q)
+        else:
+            self.q, self.k, self.v = inputs
+            if any(tuple(t.shape) != tuple(shape) or t.dtype != torch.bfloat16 or not t.is_contiguous()
+                   for t in inputs):
+                raise ValueError(f"graph inputs must be contiguous bf16 tensors of shape {tuple(shape)}")
         self.graph = None
         self._warmup = warmup
         self._scope = f"graph{next(_SCOPE_IDS)}"
@@ -151,3 +160,81 @@ class StreamedSparseAttention:
         for st in self.streams:
             cur.wait_stream(st)
         return hout
+
+
+class ConcurrentSparseAttention:
+    """One SparsePR layer on device-resident ``[1,H,N,D]`` bf16 inputs, run as
+    ``chunks`` captured graphs over contiguous head ranges, replayed
+    concurrently on their own streams.
+
+    Heads are independent in every step of the layer, but several steps are
+    latency-bound and occupy few SMs (the Jacobi eigensolver runs one CTA per
+    head; the small per-head linear algebra and the sort kernels are short).
+    Two head chains replayed together let some of one chain's latency-bound
+    kernels run beside the other chain's; the attention kernel itself holds an
+    SM's whole shared memory and tensor memory, so nothing runs beside it
+    (staggering the chains so one routes while the other attends was measured
+    and serialised completely).  The graphs read views of
+    one set of static input buffers (``load`` copies the inputs once) and each
+    starts its k-means from its rows of the all-heads cold-start draw, so the
+    outputs equal one all-heads call.  ``replay()`` returns the per-chunk
+    outputs (head ranges in order); ``output()`` concatenates them.
+    """
+
+    def __init__(self, shape, config: N8V6Config, device: torch.device, chunks: int = 2, warmup: int = 2,
+                 head_offset: int = 0, total_heads: int | None = None):
+        """``head_offset`` / ``total_heads``: these heads are rows
+        ``[head_offset, head_offset + H)`` of a ``total_heads``-head layer (a
+        rank's shard); the cold-start draw is that layer's."""
+        b, h, n, d = shape
+        total = h if total_heads is None else int(total_heads)
+        if b != 1:
+            raise ValueError("concurrent layers take B=1")
+        chunks = max(1, min(int(chunks), h))
+        bounds = [h * i // chunks for i in range(chunks + 1)]
+        self.ranges = [(bounds[i], bounds[i + 1]) for i in range(chunks) if bounds[i + 1] > bounds[i]]
+        self.device = device
+        self.q = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.k = torch.zeros_like(self.q)
+        self.v = torch.zeros_like(self.q)
+        self.graphs = []
+        for h0, h1 in self.ranges:
+            g = GraphedSparseAttention((1, h1 - h0, n, d), config, device, warmup,
+                                       inputs=(self.q[:, h0:h1], self.k[:, h0:h1], self.v[:, h0:h1]))
+            rows = g.init_rows(head_offset + h0, total)
+            g.k_init.copy_(rows[0])
+            g.q_init.copy_(rows[1])
+            self.graphs.append(g)
+        self.streams = [torch.cuda.Stream(device) for _ in self.graphs]
+
+    def capture(self):
+        for g in self.graphs:
+            g.capture()
+        return self
+
+    def load(self, q, k, v):
+        self.q.copy_(q, non_blocking=True)
+        self.k.copy_(k, non_blocking=True)
+        self.v.copy_(v, non_blocking=True)
+
+    def replay(self):
+        if any(g.graph is None for g in self.graphs):
+            self.capture()
+        cur = torch.cuda.current_stream(self.device)
+        for st in self.streams:
+            st.wait_stream(cur)
+        for g, st in zip(self.graphs, self.streams):
+            with torch.cuda.stream(st):
+                g.graph.replay()
+        for st in self.streams:
+            cur.wait_stream(st)
+        return [g.out for g in self.graphs]
+
+    def output(self):
+        """All heads' repaired output, ``[1,H,N,D]`` (a copy)."""
+        return torch.cat([g.out for g in self.graphs], dim=1)
+
+    def __call__(self, q, k, v):
+        self.load(q, k, v)
+        self.replay()
+        return self.output()

@@ -430,3 +430,20 @@ def test_top_p_budgets_route_and_layer_match_oracle(cuda):
     torch.cuda.synchronize()
     assert isinstance(g.density, torch.Tensor) and abs(float(g.density) - density) < 1e-6
     _close(got.view(2, -1, 128), out.view(2, -1, 128))
+
+
+def test_concurrent_head_chains_equal_one_graph(cuda):
+    """Head ranges as concurrent graphs on their own streams: the same bits as
+    one all-heads graph (every step of the layer is per head)."""
+    from sparsepr_b200.graph import ConcurrentSparseAttention, GraphedSparseAttention
+
+    cfg = _cfg()
+    q, k, v = (t.to(cuda) for t in synthetic_qkv(3, 128, (4, 8, 16), dtype=torch.bfloat16))
+    one = GraphedSparseAttention(q.shape, cfg, cuda).capture()
+    ref = one(q, k, v).clone()
+    conc = ConcurrentSparseAttention(q.shape, cfg, cuda, chunks=2).capture()
+    got = conc(q, k, v)
+    again = conc(q, k, v)
+    torch.cuda.synchronize()
+    assert [r for r in conc.ranges] == [(0, 1), (1, 3)]
+    assert torch.equal(got, ref) and torch.equal(again, ref)
