@@ -106,7 +106,7 @@ def _dist():
     return world, rank, local
 
 
-ATTN_DRAM_BYTES_PER_HEAD = (278.07e6 + 63.96e6) / 4
+ATTN_DRAM_BYTES_PER_HEAD = (272.19e6 + 64.94e6) / 4
 
 
 def _print_kernel_table(step, q, k, v, dev):
@@ -332,8 +332,8 @@ def run_b200(args):
             "roofline": {"kernel": "block_sparse_attn_kernel", "bound": "tensor", "achieved": achieved,
                          "peak": sustained, "peak_source": f"bf16_tflops_sustained ({src})", "unit": "TFLOP/s",
                          "frac": achieved / sustained,
-                         # DRAM bytes per launch: ncu capture of the 4-head case (278 MB read +
-                         # 64 MB written), scaled by heads (inputs and output are read/written once).
+                         # DRAM bytes per launch: ncu capture of the 4-head case (272 MB read +
+                         # 65 MB written), scaled by heads (inputs and output are read/written once).
                          "traffic": ATTN_DRAM_BYTES_PER_HEAD * local_heads, "traffic_source": "ncu, 4-head capture scaled",
                          "attn_ms": attn_ms,
                          "attn_share_of_step": attn_ms / ms},
