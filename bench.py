@@ -258,6 +258,7 @@ def run_b200(args):
     # `--graph-chunks` concurrent graph chains (head ranges on their own streams).
     g = ConcurrentSparseAttention(q.shape, cfg, dev, chunks=args.graph_chunks, warmup=max(1, args.warmup),
                                   head_offset=h0, total_heads=heads)
+    n_graphs = len(g.graphs)
     g.load(q, k, v)
     g.capture()
     for _ in range(args.warmup):
@@ -322,7 +323,7 @@ def run_b200(args):
                        "probe_rows": 64, "repair_rank": 16, "parallelism": f"heads-sharded x{world}",
                        "l2": "inputs (3 x 774 MB bf16 per 40 heads) exceed the 126 MB L2; no flush"},
             "kept_tflop_per_step": kept / 1e12,
-            "timing": f"CUDA-graph replay of the whole layer ({len(g.graphs)} concurrent head-range graphs per step); "
+            "timing": f"CUDA-graph replay of the whole layer ({n_graphs} concurrent head-range graphs per step); "
                       "eager launches (one stream) in eager_ms_per_step",
             "eager_ms_per_step": eager_ms,
             "e2e": {"value": kept / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
