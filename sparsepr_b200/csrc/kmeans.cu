@@ -109,7 +109,12 @@ __global__ void label_scatter_kernel(const int32_t* __restrict__ labels, int64_t
 
 // ---------------------------------------------------------------------------
 // Segmented mean over the sorted order (optionally fused with the permute).
-// One warp per cluster; each lane streams 16-byte chunks of rows.
+// `wpc` warps of one block per cluster (a power of two dividing the block's
+// warps); warp w of a cluster takes rows beg + w*rpw + sub + m*(wpc*rpw),
+// each lane streaming one 16-byte chunk of a row.  Large clusters thus spread
+// their gather over several warps instead of one serial chain, and the
+// partial sums are reduced in a fixed order (row groups, then warps), so the
+// result does not depend on scheduling.
 // ---------------------------------------------------------------------------
 
 template <typename T>
@@ -133,23 +138,24 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
                                       const float* __restrict__ fallback, float* __restrict__ means,
                                       T* __restrict__ x_perm, int mode, int round_dtype,
                                       float* __restrict__ shift_out, const int* __restrict__ done,
-                                      int64_t total) {
-  if (done && *done) return;
+                                      int64_t total, int wpc) {
+  if (done && *done) return;  // launch-uniform
   constexpr int E = 16 / sizeof(T);
   extern __shared__ float sh_acc[];  // [warps][d]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
-  const int64_t gw = (int64_t)blockIdx.x * warps + warp;
-  if (gw >= total) return;  // warp-uniform
-  const int64_t b = gw / k;
-  const int c = (int)(gw % k);
+  const int wi = warp & (wpc - 1);  // warp within its cluster
+  const int64_t gc = ((int64_t)blockIdx.x * warps + warp) / wpc;
+  const bool valid = gc < total;    // warp-uniform; every warp still reaches the block barrier
+  const int64_t b = valid ? gc / k : 0;
+  const int c = valid ? (int)(gc % k) : 0;
   float* acc_sh = sh_acc + warp * d;
   const int cpr = d / E;                // 16-byte chunks per row
   const int rpw = 32 / cpr;             // rows per warp step
   const int sub = lane / cpr, ch = lane % cpr;
-  const bool active = sub < rpw;
-  const int32_t beg = offsets[b * (k + 1) + c];
-  const int32_t end = offsets[b * (k + 1) + c + 1];
+  const bool active = valid && sub < rpw;
+  const int32_t beg = valid ? offsets[b * (k + 1) + c] : 0;
+  const int32_t end = valid ? offsets[b * (k + 1) + c + 1] : 0;
   const T* xb = x + b * n * d;
   const int32_t* ob = order + b * n;
   float acc[E];
@@ -159,12 +165,13 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
     // Four rows per lane group in flight: the indices first, then the rows
     // (the gather is latency-bound), accumulated in token order.
     constexpr int U = 4;
-    for (int32_t s0 = beg + sub; s0 < end; s0 += U * rpw) {
+    const int stride = rpw * wpc;
+    for (int32_t s0 = beg + wi * rpw + sub; s0 < end; s0 += U * stride) {
       int32_t tt[U];
       uint4 vv[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int32_t s = s0 + u * rpw;
+        const int32_t s = s0 + u * stride;
         tt[u] = s < end ? ob[s] : -1;
       }
 #pragma unroll
@@ -173,7 +180,7 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         if (tt[u] < 0) break;
-        if (x_perm) reinterpret_cast<uint4*>(x_perm + b * n * d + (int64_t)(s0 + u * rpw) * d)[ch] = vv[u];
+        if (x_perm) reinterpret_cast<uint4*>(x_perm + b * n * d + (int64_t)(s0 + u * stride) * d)[ch] = vv[u];
         float f[E];
         unpack16<T>(vv[u], f);
 #pragma unroll
@@ -181,7 +188,7 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
       }
     }
   }
-  // Reduce the rpw row groups through shared memory in a fixed order.
+  // Reduce the rpw row groups of this warp through shared memory in a fixed order.
   for (int i = lane; i < d; i += 32) acc_sh[i] = 0.f;
   __syncwarp();
   for (int g = 0; g < rpw; ++g) {
@@ -191,13 +198,17 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
     }
     __syncwarp();
   }
+  if (wpc > 1) __syncthreads();  // block-uniform
+  if (!valid || wi != 0) return;
   const int32_t cnt = end - beg;
   float* out = means + (b * k + c) * (int64_t)d;
   float local_shift = 0.f;
   for (int i = lane; i < d; i += 32) {
+    float sum = acc_sh[i];
+    for (int w = 1; w < wpc; ++w) sum += acc_sh[w * d + i];  // the cluster's warps in order
     float v;
     if (cnt > 0) {
-      v = acc_sh[i] / (float)cnt;
+      v = sum / (float)cnt;
     } else {
       v = fallback ? fallback[(b * k + c) * (int64_t)d + i] : 0.f;
     }
@@ -295,11 +306,16 @@ template <typename T>
 static int launch_segmented_mean(const T* x, const int32_t* order, const int32_t* offsets, int64_t bh,
                                  int64_t n, int d, int k, const float* fallback, float* means, T* x_perm,
                                  int mode, int round_dtype, float* shift, const int* done, cudaStream_t st) {
+  // Warps per cluster: about one per 48 rows of an average cluster, a power of two <= 8.
   const int warps = 8;
+  const int64_t avg = n / k;
+  int wpc = 1;
+  while (wpc < warps && avg >= 48 * 2 * wpc) wpc *= 2;
   const int64_t total = bh * k;
-  dim3 grid((unsigned)((total + warps - 1) / warps));
+  const int64_t cpb = warps / wpc;  // clusters per block
+  dim3 grid((unsigned)((total + cpb - 1) / cpb));
   segmented_mean_kernel<T><<<grid, warps * 32, warps * d * sizeof(float), st>>>(
-      x, order, offsets, n, d, k, fallback, means, x_perm, mode, round_dtype, shift, done, total);
+      x, order, offsets, n, d, k, fallback, means, x_perm, mode, round_dtype, shift, done, total, wpc);
   return check_launch("segmented mean");
 }
 
