@@ -10,79 +10,129 @@ namespace spr {
 constexpr int kCholMax = 128;
 constexpr int kCholLd = kCholMax + 1;
 
-__global__ void __launch_bounds__(256)
-chol_solve_kernel(const float* __restrict__ a, const float* __restrict__ rhs, int m, int nrhs,
-                  float* __restrict__ x) {
-  extern __shared__ float sh_l[];  // [m][kCholLd], lower triangle = L
-  const int64_t b = blockIdx.x;
-  const float* A = a + b * (int64_t)m * m;
-  for (int idx = threadIdx.x; idx < m * m; idx += blockDim.x) {
-    const int i = idx / m, j = idx % m;
-    sh_l[i * kCholLd + j] = A[idx];
-  }
-  __syncthreads();
-  // Cholesky-Banachiewicz, one column per step: L[j][j], then L[i][j] for i > j in parallel.
-  for (int j = 0; j < m; ++j) {
-    if (threadIdx.x == 0) {
-      float s = sh_l[j * kCholLd + j];
-      for (int kk = 0; kk < j; ++kk) s -= sh_l[j * kCholLd + kk] * sh_l[j * kCholLd + kk];
-      sh_l[j * kCholLd + j] = sqrtf(s);  // NaN when A is not positive definite
-    }
-    __syncthreads();
-    const float djj = sh_l[j * kCholLd + j];
-    for (int i = j + 1 + threadIdx.x; i < m; i += blockDim.x) {
-      float s = sh_l[i * kCholLd + j];
-      for (int kk = 0; kk < j; ++kk) s -= sh_l[i * kCholLd + kk] * sh_l[j * kCholLd + kk];
-      sh_l[i * kCholLd + j] = s / djj;
-    }
-    __syncthreads();
-  }
-  // One right-hand-side column per thread: L y = b, then L^T x = y (in place).
-  for (int col = threadIdx.x; col < nrhs; col += blockDim.x) {
-    const float* B = rhs + b * (int64_t)m * nrhs + col;
-    float* X = x + b * (int64_t)m * nrhs + col;
-    for (int i = 0; i < m; ++i) {
-      float s = B[(int64_t)i * nrhs];
-      for (int kk = 0; kk < i; ++kk) s -= sh_l[i * kCholLd + kk] * X[(int64_t)kk * nrhs];
-      X[(int64_t)i * nrhs] = s / sh_l[i * kCholLd + i];
-    }
-    for (int i = m - 1; i >= 0; --i) {
-      float s = X[(int64_t)i * nrhs];
-      for (int kk = i + 1; kk < m; ++kk) s -= sh_l[kk * kCholLd + i] * X[(int64_t)kk * nrhs];
-      X[(int64_t)i * nrhs] = s / sh_l[i * kCholLd + i];
-    }
-  }
-}
-
 // In-place Cholesky of the m x m matrix in shared memory (row stride ld; the
-// lower triangle becomes L).  Returns false (for every thread) when a pivot is
-// not positive and finite.  Block-wide: every thread of the CTA calls it.
-__device__ bool chol_factor_smem(float* L, int m, int ld) {
+// lower triangle becomes L), right-looking: per column j the pivot s = a_jj,
+// then the trailing lower triangle a_ik -= a_ij a_kj / s (k in (j, i]) in
+// parallel, and column j is divided by sqrt(s) one step later (the next
+// update no longer reads it): two barriers per column.  A pivot that is not
+// positive and finite makes the result false; with nan_on_fail the pivot
+// stays sqrt(s) (NaN for s < 0, which then propagates into a solve),
+// otherwise it becomes 1.  Block-wide: every thread of the CTA calls it.
+__device__ bool chol_factor_smem(float* L, int m, int ld, bool nan_on_fail = false) {
   __shared__ int s_bad;
+  __shared__ float s_inv_piv;
   if (threadIdx.x == 0) s_bad = 0;
-  __syncthreads();
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5, ny = blockDim.x >> 5;
   for (int j = 0; j < m; ++j) {
     if (threadIdx.x == 0) {
       float s = L[j * ld + j];
-      for (int kk = 0; kk < j; ++kk) s -= L[j * ld + kk] * L[j * ld + kk];
       if (!(s > 0.f) || !isfinite(s)) {
         s_bad = 1;
-        s = 1.f;
+        if (!nan_on_fail) s = 1.f;
       }
       L[j * ld + j] = sqrtf(s);
+      s_inv_piv = 1.f / s;
     }
     __syncthreads();
-    const float djj = L[j * ld + j];
-    for (int i = j + 1 + threadIdx.x; i < m; i += blockDim.x) {
-      float s = L[i * ld + j];
-      for (int kk = 0; kk < j; ++kk) s -= L[i * ld + kk] * L[j * ld + kk];
-      L[i * ld + j] = s / djj;
+    const float inv_s = s_inv_piv;
+    // Trailing update (rows i > j, columns j < k <= i) with the unscaled column j.
+    for (int i = j + 1 + ty; i < m; i += ny) {
+      const float lij = L[i * ld + j] * inv_s;
+      for (int k = j + 1 + tx; k <= i; k += 32) L[i * ld + k] = fmaf(-lij, L[k * ld + j], L[i * ld + k]);
+    }
+    if (j > 0) {  // scale the previous column, which this update did not read
+      const float pd = L[(j - 1) * ld + (j - 1)];
+      for (int i = j + threadIdx.x; i < m; i += blockDim.x) L[i * ld + (j - 1)] /= pd;
     }
     __syncthreads();
   }
   const bool ok = s_bad == 0;
   __syncthreads();
   return ok;
+}
+
+// A X = B per system: L in shared memory, then forward and back substitution
+// with the right-hand sides staged in shared memory (one column per thread,
+// in blocks of blockDim.x columns).
+__global__ void __launch_bounds__(256)
+chol_solve_kernel(const float* __restrict__ a, const float* __restrict__ rhs, int m, int nrhs,
+                  float* __restrict__ x) {
+  extern __shared__ float sh_l[];  // [m][kCholLd] L, then [m][blockDim.x] right-hand sides
+  const int nt = blockDim.x;
+  float* XS = sh_l + m * kCholLd;
+  const int64_t b = blockIdx.x;
+  const float* A = a + b * (int64_t)m * m;
+  for (int idx = threadIdx.x; idx < m * m; idx += nt) {
+    const int i = idx / m, j = idx % m;
+    sh_l[i * kCholLd + j] = A[idx];
+  }
+  __syncthreads();
+  chol_factor_smem(sh_l, m, kCholLd, /*nan_on_fail=*/true);
+  for (int c0 = 0; c0 < nrhs; c0 += nt) {
+    const int nc = min(nt, nrhs - c0);
+    const float* B = rhs + b * (int64_t)m * nrhs + c0;
+    float* X = x + b * (int64_t)m * nrhs + c0;
+    for (int idx = threadIdx.x; idx < m * nc; idx += nt) {
+      const int i = idx / nc, c = idx % nc;
+      XS[i * nt + c] = B[(int64_t)i * nrhs + c];
+    }
+    __syncthreads();
+    const int col = threadIdx.x;
+    if (col < nc) {
+      // Rows in blocks of 8: the earlier rows' contributions first (eight
+      // independent accumulators per loaded value), then the 8 x 8 triangle.
+      constexpr int RB = 8;
+      for (int i0 = 0; i0 < m; i0 += RB) {  // L y = b
+        const int nb = min(RB, m - i0);
+        float acc[RB];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) acc[r] = r < nb ? XS[(i0 + r) * nt + col] : 0.f;
+        for (int kk = 0; kk < i0; ++kk) {
+          const float xk = XS[kk * nt + col];
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < nb) acc[r] = fmaf(-sh_l[(i0 + r) * kCholLd + kk], xk, acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (r < nb) {
+#pragma unroll
+            for (int q = 0; q < r; ++q) acc[r] = fmaf(-sh_l[(i0 + r) * kCholLd + i0 + q], acc[q], acc[r]);
+            acc[r] /= sh_l[(i0 + r) * kCholLd + i0 + r];
+            XS[(i0 + r) * nt + col] = acc[r];
+          }
+        }
+      }
+      for (int i1 = m; i1 > 0; i1 -= RB) {  // L^T x = y
+        const int i0 = max(0, i1 - RB), nb = i1 - i0;
+        float acc[RB];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) acc[r] = r < nb ? XS[(i0 + r) * nt + col] : 0.f;
+        for (int kk = i1; kk < m; ++kk) {
+          const float xk = XS[kk * nt + col];
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            if (r < nb) acc[r] = fmaf(-sh_l[kk * kCholLd + i0 + r], xk, acc[r]);
+        }
+#pragma unroll
+        for (int r = RB - 1; r >= 0; --r) {
+          if (r < nb) {
+#pragma unroll
+            for (int q = r + 1; q < RB; ++q)
+              if (q < nb) acc[r] = fmaf(-sh_l[(i0 + q) * kCholLd + i0 + r], acc[q], acc[r]);
+            acc[r] /= sh_l[(i0 + r) * kCholLd + i0 + r];
+            XS[(i0 + r) * nt + col] = acc[r];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < m * nc; idx += nt) {
+      const int i = idx / nc, c = idx % nc;
+      X[(int64_t)i * nrhs + c] = XS[i * nt + c];
+    }
+    __syncthreads();
+  }
 }
 
 // Cholesky-QR of x [n][r] (n, r <= 128): columns normalised to unit length,
@@ -200,8 +250,10 @@ extern "C" int spr_chol_solve(const float* a, const float* b, int64_t batch, int
     return fail(SPR_ERR_SHAPE, "chol_solve: need 0 < batch <= 65535, 1 <= m <= 128, nrhs >= 1 (batch=%lld m=%d nrhs=%d)",
                 (long long)batch, m, nrhs);
   if (x == b) return fail(SPR_ERR_ARG, "chol_solve: x must not alias b");
-  const int smem = m * kCholLd * (int)sizeof(float);
-  cudaFuncSetAttribute(chol_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kCholMax * kCholLd * 4);
+  const int smem = (m * kCholLd + m * 256) * (int)sizeof(float);
+  const cudaError_t e = cudaFuncSetAttribute(chol_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (kCholMax * kCholLd + kCholMax * 256) * 4);
+  if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "chol_solve: shared-memory opt-in: %s", cudaGetErrorString(e));
   chol_solve_kernel<<<(unsigned)batch, 256, smem, (cudaStream_t)stream>>>(a, b, m, nrhs, x);
   return check_launch("chol_solve");
 }
