@@ -125,10 +125,12 @@ using namespace spr;
 // and the token nearest to it (squared distance, ties to the lowest token
 // index; n for an empty cluster).  One warp per cluster walks the cluster's
 // tokens in sorted order (ascending token index within a cluster).  Mean:
-// lane l sums features l and l + 32 over the tokens in that fixed order.
-// Distances: lane j takes tokens j, j + 32, ... of the cluster and computes
-// each full distance against the mean in shared memory (no shuffles per
-// token); one warp argmin at the end.
+// 16-byte loads, r/4 lanes per row and 32/(r/4) rows per warp instruction,
+// eight rows per lane in flight; each lane sums its chunk over its rows in
+// sorted order, then the row groups are added in a fixed order (shuffles).
+// Distances: lane j takes tokens j, j + 32, ... of the cluster (two per
+// iteration) and computes each full distance against the mean in shared
+// memory (no shuffles per token); one warp argmin at the end.
 constexpr int kProbeWarps = 8;
 
 __global__ void __launch_bounds__(kProbeWarps * 32)
@@ -148,55 +150,73 @@ probe_representatives_kernel(const float* __restrict__ feat, const int32_t* __re
   }
   const int32_t* ob = order + b * n;
   const float* fb = feat + b * n * r;
-  const bool has0 = lane < r, has1 = lane + 32 < r;
-  float m0 = 0.f, m1 = 0.f;
-  for (int32_t i = beg; i < end; i += 4) {  // four rows in flight, summed in token order
-    float a0[4], a1[4];
+  const int cpr = r / 4;                  // float4 chunks per row
+  const int rpw = 32 / cpr;               // rows per warp instruction (r <= 64: at least 2)
+  const int q = lane % cpr, sub = lane / cpr;
+  const bool act = sub < rpw;
+  float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (act) {
+    constexpr int U = 8;
+    for (int32_t i = beg + sub; i < end; i += U * rpw) {
+      float4 a[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      a0[u] = 0.f;
-      a1[u] = 0.f;
-      if (i + u < end) {
-        const float* row = fb + (int64_t)ob[i + u] * r;
-        if (has0) a0[u] = row[lane];
-        if (has1) a1[u] = row[lane + 32];
+      for (int u = 0; u < U; ++u) {
+        const int32_t ii = i + u * rpw;
+        a[u] = ii < end ? reinterpret_cast<const float4*>(fb + (int64_t)ob[ii] * r)[q]
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        m.x += a[u].x; m.y += a[u].y; m.z += a[u].z; m.w += a[u].w;
       }
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      m0 += a0[u];
-      m1 += a1[u];
-    }
+  }
+  // Row groups sub = 0 .. rpw-1 added in order into group 0.
+  for (int g = 1; g < rpw; ++g) {
+    const float4 o = make_float4(__shfl_sync(0xffffffffu, m.x, g * cpr + q), __shfl_sync(0xffffffffu, m.y, g * cpr + q),
+                                 __shfl_sync(0xffffffffu, m.z, g * cpr + q), __shfl_sync(0xffffffffu, m.w, g * cpr + q));
+    if (sub == 0) { m.x += o.x; m.y += o.y; m.z += o.z; m.w += o.w; }
   }
   const float cnt = (float)(end - beg);
-  sh_mean[wib][lane] = __fdiv_rn(m0, cnt);
-  sh_mean[wib][lane + 32] = __fdiv_rn(m1, cnt);
+  if (sub == 0)
+    reinterpret_cast<float4*>(sh_mean[wib])[q] =
+        make_float4(__fdiv_rn(m.x, cnt), __fdiv_rn(m.y, cnt), __fdiv_rn(m.z, cnt), __fdiv_rn(m.w, cnt));
   __syncwarp();
   float best_d = INFINITY;
   int32_t best_t = (int32_t)n;
-  for (int32_t i = beg + lane; i < end; i += 32) {
-    const int32_t t = ob[i];
+  const float4* mu = reinterpret_cast<const float4*>(sh_mean[wib]);
+  // Squared distance of token t's row to the mean, in a fixed order (two chains).
+  auto dist = [&](int32_t t) {
     const float4* row = reinterpret_cast<const float4*>(fb + (int64_t)t * r);
-    const float4* mu = reinterpret_cast<const float4*>(sh_mean[wib]);
     float d0 = 0.f, d1 = 0.f;
-    for (int q = 0; q < r / 4; q += 2) {
-      const float4 x0 = row[q], c0 = mu[q];
+    for (int qq = 0; qq < cpr; qq += 2) {
+      const float4 x0 = row[qq], c0 = mu[qq];
       d0 = fmaf(x0.x - c0.x, x0.x - c0.x, d0);
       d0 = fmaf(x0.y - c0.y, x0.y - c0.y, d0);
       d0 = fmaf(x0.z - c0.z, x0.z - c0.z, d0);
       d0 = fmaf(x0.w - c0.w, x0.w - c0.w, d0);
-      if (q + 1 < r / 4) {
-        const float4 x1 = row[q + 1], c1 = mu[q + 1];
+      if (qq + 1 < cpr) {
+        const float4 x1 = row[qq + 1], c1 = mu[qq + 1];
         d1 = fmaf(x1.x - c1.x, x1.x - c1.x, d1);
         d1 = fmaf(x1.y - c1.y, x1.y - c1.y, d1);
         d1 = fmaf(x1.z - c1.z, x1.z - c1.z, d1);
         d1 = fmaf(x1.w - c1.w, x1.w - c1.w, d1);
       }
     }
-    const float d = d0 + d1;
-    if (d < best_d) {  // tokens of a lane ascend: strict keeps the lower one
-      best_d = d;
-      best_t = t;
+    return d0 + d1;
+  };
+  for (int32_t i = beg + lane; i < end; i += 64) {  // tokens i and i + 32 of this lane, ascending
+    const int32_t t0 = ob[i];
+    const bool two = i + 32 < end;
+    const int32_t t1 = two ? ob[i + 32] : t0;
+    const float da = dist(t0), db = dist(t1);
+    if (da < best_d) {  // tokens of a lane ascend: strict keeps the lower one
+      best_d = da;
+      best_t = t0;
+    }
+    if (two && db < best_d) {
+      best_d = db;
+      best_t = t1;
     }
   }
 #pragma unroll
