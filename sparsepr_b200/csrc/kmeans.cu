@@ -45,13 +45,22 @@ __global__ void label_scan_kernel(int32_t* __restrict__ counts, int k, int nchun
   const int per = (k + blockDim.x - 1) / blockDim.x;
   const int c0 = threadIdx.x * per;
   const int c1 = min(k, c0 + per);
+  // Chunk counts are read eight at a time into registers before any store,
+  // so the loads of a group overlap (a load after a store to the same array
+  // would otherwise wait for it).
+  constexpr int CB = 8;
   int32_t local = 0;
   for (int c = c0; c < c1; ++c) {
     int32_t s = 0;
-    for (int ch = 0; ch < nchunks; ++ch) {
-      int32_t v = cnt[(int64_t)ch * k + c];
-      cnt[(int64_t)ch * k + c] = s;  // exclusive within the cluster
-      s += v;
+    for (int ch0 = 0; ch0 < nchunks; ch0 += CB) {
+      int32_t v[CB];
+#pragma unroll
+      for (int u = 0; u < CB; ++u) v[u] = ch0 + u < nchunks ? cnt[(int64_t)(ch0 + u) * k + c] : 0;
+#pragma unroll
+      for (int u = 0; u < CB; ++u) {
+        if (ch0 + u < nchunks) cnt[(int64_t)(ch0 + u) * k + c] = s;  // exclusive within the cluster
+        s += v[u];
+      }
     }
     sizes[b * k + c] = s;
     local += s;
@@ -68,7 +77,14 @@ __global__ void label_scan_kernel(int32_t* __restrict__ counts, int k, int nchun
   int32_t base = sh_part[threadIdx.x] - local;
   for (int c = c0; c < c1; ++c) {
     offsets[b * (k + 1) + c] = base;
-    for (int ch = 0; ch < nchunks; ++ch) cnt[(int64_t)ch * k + c] += base;
+    for (int ch0 = 0; ch0 < nchunks; ch0 += CB) {
+      int32_t v[CB];
+#pragma unroll
+      for (int u = 0; u < CB; ++u) v[u] = ch0 + u < nchunks ? cnt[(int64_t)(ch0 + u) * k + c] : 0;
+#pragma unroll
+      for (int u = 0; u < CB; ++u)
+        if (ch0 + u < nchunks) cnt[(int64_t)(ch0 + u) * k + c] = v[u] + base;
+    }
     base += sizes[b * k + c];
   }
   if (threadIdx.x == blockDim.x - 1) offsets[b * (k + 1) + k] = sh_part[threadIdx.x];
@@ -92,18 +108,30 @@ __global__ void label_scatter_kernel(const int32_t* __restrict__ labels, int64_t
   const int32_t* lab = labels + b * n;
   int32_t* ord = order + b * n;
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int64_t base = t0; base < t1; base += 32) {
-    const int64_t t = base + lane;
-    const bool valid = t < t1;
-    const int l = valid ? lab[t] : -1 - lane;  // invalid lanes never match a real label
-    const unsigned peers = __match_any_sync(0xffffffffu, l);
-    const int rank = __popc(peers & lt_mask);
-    int pos = 0;
-    if (valid) pos = sh_cur[l] + rank;
-    __syncwarp();
-    if (valid && rank == 0) sh_cur[l] += __popc(peers);
-    __syncwarp();
-    if (valid) ord[pos] = (int32_t)t;
+  // Labels of eight 32-token steps are loaded before the steps run, so the
+  // global-load latency is paid once per eight steps.
+  constexpr int PF = 8;
+  for (int64_t g0 = t0; g0 < t1; g0 += 32 * PF) {
+    int lv[PF];
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int64_t t = g0 + 32 * u + lane;
+      lv[u] = t < t1 ? lab[t] : -1 - lane;  // invalid lanes never match a real label
+    }
+#pragma unroll
+    for (int u = 0; u < PF; ++u) {
+      const int64_t t = g0 + 32 * u + lane;
+      const bool valid = t < t1;
+      const int l = lv[u];
+      const unsigned peers = __match_any_sync(0xffffffffu, l);
+      const int rank = __popc(peers & lt_mask);
+      int pos = 0;
+      if (valid) pos = sh_cur[l] + rank;
+      __syncwarp();
+      if (valid && rank == 0) sh_cur[l] += __popc(peers);
+      __syncwarp();
+      if (valid) ord[pos] = (int32_t)t;
+    }
   }
 }
 
