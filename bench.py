@@ -284,7 +284,11 @@ def run_b200(args):
     hout = torch.empty(hq.shape, dtype=torch.bfloat16).pin_memory()
     del q, k, v, g
     torch.cuda.synchronize(dev)
-    chunk = args.e2e_chunk if local_heads % args.e2e_chunk == 0 else local_heads
+    # Heads per streamed chunk: about eight chunks per rank (5 at 40 heads, 1 at
+    # 5), so the copies of one chunk overlap the compute of the others.
+    chunk = args.e2e_chunk if args.e2e_chunk > 0 else max(1, local_heads // 8)
+    while local_heads % chunk:
+        chunk -= 1
     sg = StreamedSparseAttention(hq.shape, cfg, dev, heads_per_chunk=chunk, slots=args.e2e_slots,
                                  warmup=max(1, args.warmup)).capture()
     for _ in range(max(1, args.warmup)):
@@ -647,7 +651,8 @@ def main():
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
     ap.add_argument("--graph-chunks", type=int, default=2,
                     help="concurrent head-range graphs of the timed layer (1 = one graph for all heads)")
-    ap.add_argument("--e2e-chunk", type=int, default=5, help="heads per streamed chunk in the e2e measurement")
+    ap.add_argument("--e2e-chunk", type=int, default=0,
+                    help="heads per streamed chunk in the e2e measurement (0: about eight chunks per rank)")
     ap.add_argument("--e2e-slots", type=int, default=8, help="concurrent graph slots (streams) in the e2e measurement")
     ap.add_argument("--ulysses", action="store_true",
                     help="(torchrun, N > 1) time the sequence-sharded Ulysses variant instead of the bench line")
