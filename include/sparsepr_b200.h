@@ -323,8 +323,10 @@ int spr_selftest_bounded_wait(int* err, int code, int64_t limit_ns, void* stream
 /* ---------------------------------------------------------------- small linear algebra */
 
 /*
- * Batched symmetric eigendecomposition (cyclic two-sided Jacobi, one CTA per
- * matrix): a [batch,n,n] fp32 (symmetrised on load), n even <= 128.  Outputs
+ * Batched symmetric eigendecomposition (one CTA per matrix; n = 64, 128:
+ * Householder tridiagonalisation, multisection and twisted-factorisation
+ * eigenvectors, Jacobi for matrices with repeated eigenvalues; other n:
+ * cyclic two-sided Jacobi): a [batch,n,n] fp32 (symmetrised on load), n even <= 128.  Outputs
  * evals [batch,n] ascending and evecs [batch,n,n] with eigenvectors in the
  * columns, the torch.linalg.eigh convention.  Replaces the torch.linalg.eigh calls of
  * src/sparsepr/models/cosmos3/operator_kmeans.py:94-151 (metric_factor) and
@@ -332,6 +334,19 @@ int spr_selftest_bounded_wait(int* err, int code, int64_t limit_ns, void* stream
  */
 int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
                 void* stream);
+
+/*
+ * The same decomposition when only the `top` largest eigenpairs are used:
+ * evals [batch,n] all eigenvalues ascending; evecs [batch,n,n] holds the
+ * eigenvectors of the `top` largest eigenvalues in its last `top` columns and
+ * zeros elsewhere (n = 64 and 128; other n return all eigenvectors).  The
+ * callers of the reference take the top columns of a full torch.linalg.eigh
+ * (src/sparsepr/models/cosmos3/operator_kmeans.py:94-151, metric_factor;
+ * src/sparsepr/models/cosmos3/residual_repair.py:468-491), so the unused
+ * vectors are not formed.  1 <= top <= n, else SPR_ERR_ARG.
+ */
+int spr_sym_eig_top(const float* a, int64_t batch, int n, int top, int max_sweeps, float* evals, float* evecs,
+                    void* stream);
 
 /*
  * Batched Cholesky solve A x = b of symmetric positive definite systems:

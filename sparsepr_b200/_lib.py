@@ -61,6 +61,7 @@ PROTOTYPES = {
     "spr_block_sparse_attn_noalloc_status": (_I, [_P]),
     "spr_selftest_bounded_wait": (_I, [_P, _I, _I64, _P]),
     "spr_sym_eig": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "spr_sym_eig_top": (_I, [_P, _I64, _I, _I, _I, _P, _P, _P]),
     "spr_chol_solve": (_I, [_P, _P, _I64, _I, _I, _P, _P]),
     "spr_repair_apply": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _I, _P, _P]),
 }

@@ -338,7 +338,7 @@ constexpr int kTriThreads = 512;
 
 template <int N>
 __global__ void __launch_bounds__(kTriThreads, 1)
-sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, float* __restrict__ evecs) {
+sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, float* __restrict__ evecs, int top) {
   constexpr int n = N, ld = N + 1, G = kTriThreads / N;  // G: row groups / threads per eigenvalue
   static_assert(G >= 2 && 32 % G == 0, "size not supported");
   extern __shared__ float sh[];
@@ -507,8 +507,10 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
   }
   __syncthreads();
 
-  // 3. Eigenvector of T for lambda_j (thread j), written to column j of Z.
-  if (tid < n) {
+  // 3. Eigenvector of T for lambda_j (thread j), written to column j of Z;
+  // only the `top` largest (columns n-top .. n-1) when fewer are wanted.
+  const int jlo = n - top;
+  if (tid >= jlo && tid < n) {
     const int j = tid;
     const float lam = s_lam[j];
     float lp[N], um[N], dpv[N];
@@ -555,7 +557,7 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
   // loops); a vector that collapses into its group hands the matrix back.
   {
     const float gtol = fmaxf(1e-5f * tnorm, 4.f * pivmin);  // (near-)repeated eigenvalues only
-    int g0 = 0;
+    int g0 = jlo;
     while (g0 < n) {
       int g1 = g0 + 1;
       while (g1 < n && s_lam[g1] - s_lam[g1 - 1] <= gtol) ++g1;
@@ -600,7 +602,7 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
     const float beta = s_beta[k];
     if (beta == 0.f) continue;  // block-uniform
     const int m = n - 1 - k;
-    {  // y_col = v . Z[k+1.., col]: row group grp
+    if (col >= jlo) {  // y_col = v . Z[k+1.., col]: row group grp
       const float* vk = A + (k + 1) * ld + k;
       const float* zc = Z + (k + 1) * ld + col;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -615,7 +617,7 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
       s_part[grp * N + col] = (a0 + a1) + (a2 + a3);
     }
     __syncthreads();
-    {
+    if (col >= jlo) {
       float y = 0.f;
 #pragma unroll
       for (int g = 0; g < G; ++g) y += s_part[g * N + col];
@@ -631,7 +633,27 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
   // 6. One Newton-Schulz step towards the nearest orthogonal matrix,
   // Z <- Z (3I - Z^T Z) / 2: an orthogonality error E becomes O(E^2).  The
   // reflectors are no longer needed, so A holds C = (3I - Z^T Z) / 2.
-  {
+  if (top < n) {
+    // Only the top columns: C = (3I - Zt^T Zt)/2 (top x top) in A, then Zt C.
+    for (int idx = tid; idx < top * top; idx += kTriThreads) {
+      const int i = idx / top, j = idx % top;
+      float g = 0.f;
+      for (int r = 0; r < n; ++r) g = fmaf(Z[r * ld + jlo + i], Z[r * ld + jlo + j], g);
+      A[i * ld + j] = (i == j ? 1.5f : 0.f) - 0.5f * g;
+    }
+    __syncthreads();
+    float nz[(N * N + kTriThreads - 1) / kTriThreads];
+    int cnt = 0;
+    for (int idx = tid; idx < n * top; idx += kTriThreads, ++cnt) {
+      const int r = idx / top, j = idx % top;
+      float acc = 0.f;
+      for (int c = 0; c < top; ++c) acc = fmaf(Z[r * ld + jlo + c], A[c * ld + j], acc);
+      nz[cnt] = acc;
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int idx = tid; idx < n * top; idx += kTriThreads, ++cnt) Z[(idx / top) * ld + jlo + idx % top] = nz[cnt];
+  } else {
     // Register tiles: thread (ib, jb) = (warp * 2 + lane / 16, lane % 16) owns
     // rows ib + 32v (v < n/32) and columns jb + 16u (u < n/16); for a fixed u
     // a half-warp reads 16 consecutive columns, the other operand is a broadcast.
@@ -695,7 +717,7 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
   const bool bad = s_bad != 0;
   for (int idx = tid; idx < n * n; idx += kTriThreads) {
     const int i = idx / n, j = idx % n;
-    out[i * n + j] = Z[i * ld + j];
+    out[i * n + j] = j >= jlo ? Z[i * ld + j] : 0.f;
   }
   if (tid < n) ev[tid] = (bad && tid == 0) ? __int_as_float(0x7fc00000) : s_lam[tid];
 }
@@ -704,8 +726,8 @@ sym_eig_tri_kernel(const float* __restrict__ a_in, float* __restrict__ evals, fl
 
 using namespace spr;
 
-extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
-                           void* stream) {
+static int sym_eig_launch(const float* a, int64_t batch, int n, int top, int max_sweeps, float* evals,
+                          float* evecs, void* stream) {
   if (batch <= 0 || batch > 65535 || n < 2 || n > kEigMax || (n & 1))
     return fail(SPR_ERR_SHAPE, "sym_eig: need 0 < batch <= 65535 and even 2 <= n <= 128, got batch=%lld n=%d",
                 (long long)batch, n);
@@ -723,7 +745,7 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
     auto tri = n == 64 ? sym_eig_tri_kernel<64> : sym_eig_tri_kernel<128>;
     cudaError_t e = cudaFuncSetAttribute(tri, cudaFuncAttributeMaxDynamicSharedMemorySize, tri_smem);
     if (e != cudaSuccess) return fail(SPR_ERR_LAUNCH, "sym_eig: shared-memory opt-in: %s", cudaGetErrorString(e));
-    tri<<<(unsigned)batch, kTriThreads, tri_smem, st>>>(a, evals, evecs);
+    tri<<<(unsigned)batch, kTriThreads, tri_smem, st>>>(a, evals, evecs, top);
     const int big = n * (n + 1) * (int)sizeof(float);
     auto kern = n == 64 ? sym_eig_big_kernel<64> : sym_eig_big_kernel<128>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
@@ -745,3 +767,14 @@ extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps,
   }
 }
 
+
+extern "C" int spr_sym_eig(const float* a, int64_t batch, int n, int max_sweeps, float* evals, float* evecs,
+                           void* stream) {
+  return sym_eig_launch(a, batch, n, n, max_sweeps, evals, evecs, stream);
+}
+
+extern "C" int spr_sym_eig_top(const float* a, int64_t batch, int n, int top, int max_sweeps, float* evals,
+                               float* evecs, void* stream) {
+  if (top < 1 || top > n) return fail(SPR_ERR_ARG, "sym_eig_top: top=%d must be in [1, n=%d]", top, n);
+  return sym_eig_launch(a, batch, n, top, max_sweeps, evals, evecs, stream);
+}

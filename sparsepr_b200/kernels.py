@@ -469,9 +469,11 @@ def repair_apply(base: torch.Tensor, state, alpha: float, rows: torch.Tensor | N
     return out
 
 
-def sym_eig(a: torch.Tensor, max_sweeps: int = 15):
+def sym_eig(a: torch.Tensor, max_sweeps: int = 15, top: int | None = None):
     """Batched symmetric eigendecomposition of [B,n,n] (n even <= 128):
-    (eigenvalues ascending [B,n], eigenvectors in columns [B,n,n]), fp32."""
+    (eigenvalues ascending [B,n], eigenvectors in columns [B,n,n]), fp32.
+    ``top``: only the eigenvectors of the ``top`` largest eigenvalues are
+    formed (the last ``top`` columns; zeros elsewhere for n = 64, 128)."""
     dev = _cuda(a)
     b, n, n2 = a.shape
     if n != n2:
@@ -480,7 +482,10 @@ def sym_eig(a: torch.Tensor, max_sweeps: int = 15):
     evals = torch.empty((b, n), dtype=torch.float32, device=dev)
     evecs = torch.empty((b, n, n), dtype=torch.float32, device=dev)
     _count(1)
-    _lib.call("spr_sym_eig", _p(a), b, n, int(max_sweeps), _p(evals), _p(evecs), _stream(dev))
+    if top is None:
+        _lib.call("spr_sym_eig", _p(a), b, n, int(max_sweeps), _p(evals), _p(evecs), _stream(dev))
+    else:
+        _lib.call("spr_sym_eig_top", _p(a), b, n, int(top), int(max_sweeps), _p(evals), _p(evecs), _stream(dev))
     return evals, evecs
 
 

@@ -231,7 +231,7 @@ def metric_factor(metric: torch.Tensor, rank: int) -> torch.Tensor:
         raise RuntimeError(f"Expected batched square metrics, got {tuple(metric.shape)}.")
     if rank <= 0 or rank > metric.shape[-1]:
         raise RuntimeError(f"rank must be in [1, {metric.shape[-1]}], got {rank}.")
-    evals, evecs = K.sym_eig(metric.float())  # symmetrised inside the kernel
+    evals, evecs = K.sym_eig(metric.float(), top=rank)  # symmetrised inside the kernel
     evals = evals[:, -rank:].clamp_min(0.0)
     evecs = evecs[:, :, -rank:]
     norm = evals.mean(dim=1, keepdim=True).clamp_min(1e-12)
@@ -399,7 +399,7 @@ def fit_reduced_rank_residual(x_fit, y_fit, weights, rank: int, ridge: float):
     gram = torch.bmm(xw, xw.transpose(1, 2))
     gram.diagonal(dim1=1, dim2=2).add_(float(ridge))
     dual = K.chol_solve(gram, yw)
-    evals, evecs = K.sym_eig(torch.bmm(yw, yw.transpose(1, 2)))
+    evals, evecs = K.sym_eig(torch.bmm(yw, yw.transpose(1, 2)), top=rank)
     evecs = evecs[:, :, -rank:]
     scales = evals[:, -rank:].clamp_min(1e-20).rsqrt().unsqueeze(1)
     basis = (torch.bmm(yw.transpose(1, 2), evecs) * scales).contiguous()

@@ -255,6 +255,35 @@ def test_sym_eig_matches_lapack(cuda, n):
     assert torch.all(w[:, 1:] >= w[:, :-1])
 
 
+@pytest.mark.parametrize("n,top", [(128, 64), (128, 48), (64, 16), (64, 64)])
+def test_sym_eig_top_matches_lapack(cuda, n, top):
+    """Top-``top`` eigenpairs only: all eigenvalues as the full call returns
+    them, the last ``top`` columns hold orthonormal eigenvectors (residual
+    and orthogonality as in the full test), the other columns are zero; the
+    zero matrix (handed to the Jacobi fallback) still yields valid pairs."""
+    g = torch.Generator().manual_seed(n + top)
+    x = torch.randn(4, 3 * n + 7, n, generator=g)
+    a = x.transpose(1, 2) @ x / x.shape[1]
+    a[1] = a[1] * 0
+    w_full, _ = K.sym_eig(a.to(cuda))
+    w, v = K.sym_eig(a.to(cuda), top=top)
+    assert torch.equal(w.cpu(), w_full.cpu())
+    w, v = w.cpu().double(), v.cpu().double()
+    wr = torch.linalg.eigvalsh(a.double())
+    scale = wr.abs().amax(dim=1, keepdim=True).clamp_min(1.0)
+    assert ((w - wr).abs() / scale).max().item() < 2e-4
+    vt, wt = v[:, :, n - top:], w[:, n - top:]
+    resid = (a.double() @ vt - vt * wt.unsqueeze(1)).abs().amax(dim=(1, 2)) / scale.squeeze(1)
+    assert resid.max().item() < 1e-4
+    eye = torch.eye(top, dtype=torch.float64)
+    assert (vt.transpose(1, 2) @ vt - eye).abs().max().item() < 1e-4
+    if top < n:
+        zero_cols = v[[0, 2, 3], :, : n - top]  # matrix 1 went through the full fallback
+        assert torch.count_nonzero(zero_cols).item() == 0
+    with pytest.raises(RuntimeError):
+        K.sym_eig(a.to(cuda), top=n + 1)
+
+
 @pytest.mark.parametrize("precision", ["tf32", "fp32"])
 def test_assign_many_items_per_cta(cuda, precision):
     """Persistent assignment with many point tiles per CTA and 8 centroid tiles
