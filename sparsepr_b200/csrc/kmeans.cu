@@ -192,19 +192,29 @@ __global__ void segmented_mean_kernel(const T* __restrict__ x, const int32_t* __
   if (active) {
     // Four rows per lane group in flight: the indices first, then the rows
     // (the gather is latency-bound), accumulated in token order.
+    // The next batch's row indices are loaded while this batch's rows are in
+    // flight, so each batch waits for one memory round trip instead of two.
     constexpr int U = 4;
     const int stride = rpw * wpc;
+    int32_t tn[U];
+    {
+      const int32_t s0 = beg + wi * rpw + sub;
+#pragma unroll
+      for (int u = 0; u < U; ++u) tn[u] = s0 + u * stride < end ? ob[s0 + u * stride] : -1;
+    }
     for (int32_t s0 = beg + wi * rpw + sub; s0 < end; s0 += U * stride) {
       int32_t tt[U];
       uint4 vv[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int32_t s = s0 + u * stride;
-        tt[u] = s < end ? ob[s] : -1;
-      }
+      for (int u = 0; u < U; ++u) tt[u] = tn[u];
 #pragma unroll
       for (int u = 0; u < U; ++u)
         if (tt[u] >= 0) vv[u] = reinterpret_cast<const uint4*>(xb + (int64_t)tt[u] * d)[ch];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int32_t s = s0 + U * stride + u * stride;
+        tn[u] = s < end ? ob[s] : -1;
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         if (tt[u] < 0) break;
