@@ -111,6 +111,125 @@ select_budget_kernel(const float* __restrict__ scores, const int32_t* __restrict
   if (threadIdx.x == 0) sel_counts[row] = nsel;
 }
 
+// Warp-per-row selector for ck <= 1024 (same keys, order and rule as
+// select_budget_kernel, so the result is identical).  Position i = e * 32 +
+// lane of the padded row (P = 32 E entries) lives in register e of `lane`; the
+// bitonic network's strides >= 32 compare two registers of one lane, strides
+// < 32 two lanes (shuffles).  The sorted positions' costs are scanned e-major
+// with warp scans; per-id flags go through shared memory for the ascending
+// compaction.  No block barriers.
+constexpr int kSelWarps = 8;
+
+template <int E>
+__global__ void __launch_bounds__(kSelWarps * 32)
+select_budget_warp_kernel(const float* __restrict__ scores, const int32_t* __restrict__ sizes,
+                          const int32_t* __restrict__ budgets, int64_t rows, int cq, int ck,
+                          uint8_t* __restrict__ routed, int32_t* __restrict__ sel_ids,
+                          int32_t* __restrict__ sel_counts) {
+  constexpr int P = 32 * E;
+  __shared__ uint8_t sh_flag[kSelWarps][P];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * kSelWarps + w;
+  if (row >= rows) return;  // warp-uniform; no block barrier below
+  const int64_t b = row / cq;
+  const int q = (int)(row % cq);
+  const float* sr = scores + row * ck;
+  unsigned long long key[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    key[e] = i < ck ? (((unsigned long long)float_order_desc(sr[i]) << 32) | (uint32_t)i) : ~0ull;
+  }
+  // Bitonic sort ascending on (descending score, ascending id).
+#pragma unroll
+  for (int size = 2; size <= P; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= 32) {
+        const int es = stride / 32;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e & es) == 0) {
+            const bool up = (((e * 32 + lane) & size) == 0);
+            const unsigned long long a = key[e], c = key[e | es];
+            if ((a > c) == up) { key[e] = c; key[e | es] = a; }
+          }
+        }
+      } else {
+        const bool lo = (lane & stride) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const bool up = (((e * 32 + lane) & size) == 0);
+          const unsigned long long v = key[e];
+          const uint32_t whi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), stride);
+          const uint32_t wlo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, stride);
+          const unsigned long long o = ((unsigned long long)whi << 32) | wlo;
+          const unsigned long long mn = v < o ? v : o, mx = v < o ? o : v;
+          key[e] = (lo == up) ? mn : mx;
+        }
+      }
+    }
+  }
+  const int32_t budget = budgets[row];
+  const int32_t* sz = sizes + b * ck;
+  // Costs in sorted order, inclusive prefix of the positive ones, e-major.
+  int32_t cost[E];
+  bool keep[E];
+  int32_t carry = 0, cnt_total = 0, cost_total = 0, valid_total = 0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const uint32_t id = (uint32_t)key[e];
+    const int32_t c = id < (uint32_t)ck ? sz[id] : 0;
+    cost[e] = c;
+    int32_t x = c > 0 ? c : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    const int32_t cum = carry + x;
+    carry += __shfl_sync(0xffffffffu, x, 31);
+    keep[e] = c > 0 && cum <= budget;
+    cnt_total += __popc(__ballot_sync(0xffffffffu, keep[e]));
+    valid_total += __popc(__ballot_sync(0xffffffffu, c > 0));
+    int32_t kc = keep[e] ? c : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kc += __shfl_xor_sync(0xffffffffu, kc, o);
+    cost_total += kc;
+  }
+  const bool need = budget > 0 && cost_total < budget && cnt_total < valid_total;
+  uint8_t* fl = sh_flag[w];
+#pragma unroll
+  for (int e = 0; e < E; ++e) fl[e * 32 + lane] = 0;
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const uint32_t id = (uint32_t)key[e];
+    if (id < (uint32_t)ck) fl[id] = keep[e] || (need && e * 32 + lane == cnt_total);
+  }
+  __syncwarp();
+  if (routed) {
+    uint8_t* rr = routed + (b * (cq + 1) + q + 1) * (int64_t)(ck + 1);
+    for (int i = lane; i <= ck; i += 32) rr[i] = i == 0 ? 1 : fl[i - 1];
+    if (q == 0) {
+      uint8_t* r0 = routed + b * (cq + 1) * (int64_t)(ck + 1);
+      for (int i = lane; i <= ck; i += 32) r0[i] = i == 0 ? 1 : 0;
+    }
+  }
+  // Compact selected ids in ascending cluster order.
+  int32_t* ids = sel_ids + row * ck;
+  int32_t nsel = 0;
+  for (int i0 = 0; i0 < ck; i0 += 32) {
+    const int i = i0 + lane;
+    const bool f = i < ck && fl[i];
+    const unsigned m = __ballot_sync(0xffffffffu, f);
+    if (f) ids[nsel + __popc(m & ((1u << lane) - 1u))] = i;
+    nsel += __popc(m);
+  }
+  for (int i = nsel + lane; i < ck; i += 32) ids[i] = -1;
+  if (lane == 0) sel_counts[row] = nsel;
+}
+
 }  // namespace spr
 
 using namespace spr;
@@ -119,7 +238,24 @@ extern "C" int spr_select_budget(const float* scores, const int32_t* k_sizes, co
                                  int cq, int ck, uint8_t* routed, int32_t* sel_ids, int32_t* sel_counts, void* stream) {
   if (bh <= 0 || cq <= 0 || ck <= 0 || ck > 2048)
     return fail(SPR_ERR_SHAPE, "selector: need 0 < ck <= 2048, got ck=%d", ck);
-  select_budget_kernel<<<(unsigned)(bh * cq), 1024, 0, (cudaStream_t)stream>>>(scores, k_sizes, budgets, cq, ck,
-                                                                                routed, sel_ids, sel_counts);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t rows = bh * cq;
+  const unsigned wgrid = (unsigned)((rows + kSelWarps - 1) / kSelWarps);
+  if (ck <= 1024) {  // one warp per row, keys in registers
+    int e = 1;
+    while (32 * e < ck) e <<= 1;
+    switch (e) {
+#define SPR_SEL_CASE(EE)                                                                                        \
+  case EE:                                                                                                      \
+    select_budget_warp_kernel<EE><<<wgrid, kSelWarps * 32, 0, st>>>(scores, k_sizes, budgets, rows, cq, ck,    \
+                                                                    routed, sel_ids, sel_counts);              \
+    break;
+      SPR_SEL_CASE(1) SPR_SEL_CASE(2) SPR_SEL_CASE(4) SPR_SEL_CASE(8) SPR_SEL_CASE(16) SPR_SEL_CASE(32)
+#undef SPR_SEL_CASE
+    }
+    return check_launch("selector");
+  }
+  select_budget_kernel<<<(unsigned)rows, 1024, 0, st>>>(scores, k_sizes, budgets, cq, ck, routed, sel_ids,
+                                                        sel_counts);
   return check_launch("selector");
 }
