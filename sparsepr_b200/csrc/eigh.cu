@@ -1,8 +1,12 @@
 // Batched symmetric eigendecomposition of small matrices (n <= 128, even),
-// one CTA per matrix, cyclic two-sided Jacobi with a round-robin pair
-// ordering (Golub & Van Loan, "Matrix Computations", sym.schur2 rotations and
-// the parallel-ordering cyclic Jacobi method).  Used for the role-metric
-// factors (128x128) and the repair basis (64x64 row Gram).
+// one CTA per matrix.  n = 64 and 128 (the role-metric factors, 128x128, and
+// the repair basis, 64x64 row Gram) take the tridiagonal route
+// (sym_eig_tri_kernel: Householder reduction, multisection, twisted
+// factorisation, back-transformation, one Newton-Schulz step), optionally
+// forming only the top eigenvectors; a matrix it hands back (repeated
+// eigenvalues) and every other n use cyclic two-sided Jacobi with a
+// round-robin pair ordering (Golub & Van Loan, "Matrix Computations",
+// sym.schur2 rotations and the parallel-ordering cyclic Jacobi method).
 //
 // Output matches torch.linalg.eigh's convention: eigenvalues ascending,
 // eigenvectors in the columns of a row-major [n][n] matrix.
