@@ -724,11 +724,15 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
           if (gt >= 2 && !(ok = tc::mbar_wait(&bar_d_free[db], (uint32_t)(((gt >> 1) - 1) & 1), err, 33))) break;
           tc::tc_fence_after();
           const uint32_t cbase = sc0 + st * L::kTileBytes;
+          // The last centroid tile is only as wide as its centroids (rounded up
+          // to 16): its MMAs read fewer B rows; columns past it are masked.
+          const int nt = t == ctiles - 1 ? min(kAsgN, (k - t * kAsgN + 15) & ~15) : kAsgN;
+          const uint32_t idesc_t = tc::idesc_tf32_f32(128, nt), idesc_bf_t = tc::idesc_bf16_f32(128, nt, 0);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const uint32_t dt = tmem + (uint32_t)(db * MT + mt) * 128;
             if constexpr (FOLD)
-              tc::mma_tf32(dt, tc::sw128_desc(sones, 16, 1024), tc::sw128_desc(cbase + offf, 16, 1024), kIdescAsg,
+              tc::mma_tf32(dt, tc::sw128_desc(sones, 16, 1024), tc::sw128_desc(cbase + offf, 16, 1024), idesc_t,
                            false);
             // 8 tf32 or 16 bf16 (32 bytes) per MMA K step; steps wholly inside
             // the zero padding past d are skipped.
@@ -737,10 +741,10 @@ assign_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constan
               const uint32_t off = (kb >> 7) * (kAsgM * 128) + (kb & 127);
               if constexpr (BF)
                 tc::mma_f16(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
-                            tc::sw128_desc(cbase + off, 16, 1024), kIdescAsgBf, kk > 0);
+                            tc::sw128_desc(cbase + off, 16, 1024), idesc_bf_t, kk > 0);
               else
                 tc::mma_tf32(dt, tc::sw128_desc(xbase + mt * L::kTileBytes + off, 16, 1024),
-                             tc::sw128_desc(cbase + off, 16, 1024), kIdescAsg, FOLD || kk > 0);
+                             tc::sw128_desc(cbase + off, 16, 1024), idesc_t, FOLD || kk > 0);
             }
           }
           tc::mma_commit(&bar_d_full[db]);
