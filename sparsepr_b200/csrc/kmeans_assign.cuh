@@ -30,7 +30,6 @@ constexpr int kAsgThreads = 416;
 constexpr int kAsgLoaders = 128;
 constexpr int kAsgEpilogue = 256;
 constexpr uint32_t kIdescAsg = tc::idesc_tf32_f32(128, 128);
-constexpr uint32_t kIdescAsgBf = tc::idesc_bf16_f32(128, 128, 0);  // both operands K-major
 
 template <int DP, bool SPLIT>
 struct AsgSmem {
