@@ -256,7 +256,11 @@ def run_b200(args):
     # Timed region: the whole layer captured as CUDA graphs (all kernels of the
     # step, fresh routing every replay), inputs resident in HBM; the heads run as
     # `--graph-chunks` concurrent graph chains (head ranges on their own streams).
-    g = ConcurrentSparseAttention(q.shape, cfg, dev, chunks=args.graph_chunks, warmup=max(1, args.warmup),
+    # Concurrent head-range chains help at many heads per GPU (latency-bound
+    # routing kernels of one chain overlap the other's); at a few heads per
+    # GPU one chain is faster (measured: 40 heads 2 chains < 1; 5 heads 1 < 2 < 5).
+    chains = args.graph_chunks if args.graph_chunks > 0 else (2 if local_heads >= 20 else 1)
+    g = ConcurrentSparseAttention(q.shape, cfg, dev, chunks=chains, warmup=max(1, args.warmup),
                                   head_offset=h0, total_heads=heads)
     n_graphs = len(g.graphs)
     g.load(q, k, v)
@@ -649,8 +653,9 @@ def main():
                          "4: a HunyuanVideo-architecture DiT step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--heads", type=int, default=0, help="override the head count (profiling runs)")
-    ap.add_argument("--graph-chunks", type=int, default=2,
-                    help="concurrent head-range graphs of the timed layer (1 = one graph for all heads)")
+    ap.add_argument("--graph-chunks", type=int, default=0,
+                    help="concurrent head-range graphs of the timed layer (1 = one graph for all heads; "
+                         "0: 2 at 20 or more heads per GPU, else 1)")
     ap.add_argument("--e2e-chunk", type=int, default=0,
                     help="heads per streamed chunk in the e2e measurement (0: about eight chunks per rank)")
     ap.add_argument("--e2e-slots", type=int, default=8, help="concurrent graph slots (streams) in the e2e measurement")
